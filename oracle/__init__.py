@@ -1,0 +1,194 @@
+"""CPU oracle for the torch_mcpu device hot path.
+
+TEST INFRASTRUCTURE ONLY.  tests/, the smoke check in __graft_entry__.py and
+the CPU legs of bench.py import this package as the checker.  The product
+package (torch_mcpu_b200) never imports it.
+
+The arithmetic lives in oracle.c (built by oracle/Makefile into
+oracle/build/liboracle.so); this module wraps it with numpy arrays and adds the
+numpy restatement of the tensor-parallel MLP of the reference's
+example/01_mlp_tp4/run.py:35-56,106-126 in the gated (SwiGLU) form the
+benchmark configurations use.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "build", "liboracle.so")
+_lib = None
+
+EXP_GLIBC = 0
+EXP_CR = 1
+SOFTMAX = 0
+SIGMOID = 1
+
+
+def build() -> str:
+    """Compile oracle.c with the committed Makefile (gcc only)."""
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _LIB_PATH
+
+
+def _load():
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(_LIB_PATH) or os.path.getmtime(_LIB_PATH) < os.path.getmtime(
+        os.path.join(_HERE, "oracle.c")
+    ):
+        build()
+    lib = ctypes.CDLL(_LIB_PATH)
+    P = ctypes.c_void_p
+    lib.oracle_grouped_topk.argtypes = [
+        P, ctypes.c_int, ctypes.c_int64, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+        ctypes.c_int, ctypes.c_int, ctypes.c_float, P, ctypes.c_int, ctypes.c_int,
+        P, P, P, P, ctypes.c_int,
+    ]
+    lib.oracle_grouped_topk.restype = ctypes.c_int
+    lib.oracle_silu_and_mul_bf16.argtypes = [P, ctypes.c_int64, ctypes.c_int64, P, ctypes.c_int, ctypes.c_int]
+    lib.oracle_silu_and_mul_bf16.restype = ctypes.c_int
+    lib.oracle_rms_norm_bf16.argtypes = [P, P, ctypes.c_int64, ctypes.c_int64, ctypes.c_float, P, ctypes.c_int]
+    lib.oracle_rms_norm_bf16.restype = ctypes.c_int
+    lib.oracle_sigmoid_f32.argtypes = [P, ctypes.c_int64, P, ctypes.c_int]
+    lib.oracle_sigmoid_f32.restype = None
+    _lib = lib
+    return lib
+
+
+def _ptr(a: np.ndarray | None):
+    return None if a is None else a.ctypes.data_as(ctypes.c_void_p)
+
+
+def grouped_topk(
+    gating: np.ndarray,
+    topk: int,
+    renormalize: bool,
+    num_expert_group: int,
+    topk_group: int,
+    scoring_func: str = "softmax",
+    routed_scaling_factor: float = 1.0,
+    e_score_correction_bias: np.ndarray | None = None,
+    exp_mode: int = EXP_GLIBC,
+    nthreads: int = 0,
+):
+    """Oracle grouped_topk (tests/test_grouped_topk_compile.py:15-66).
+
+    gating: [T, E] float32, or uint16 holding bf16 bits.
+    Returns (weights f32 [T, K], ids i32 [T, K], tie_rows bool [T], gaps f32 [T]).
+    """
+    lib = _load()
+    g = np.ascontiguousarray(gating)
+    if g.dtype == np.float32:
+        dt = 0
+    elif g.dtype == np.uint16:
+        dt = 1
+    else:
+        raise TypeError(f"gating must be float32 or bf16 bits (uint16), got {g.dtype}")
+    T, E = g.shape
+    bias = None
+    if e_score_correction_bias is not None:
+        bias = np.ascontiguousarray(e_score_correction_bias, dtype=np.float32)
+        assert bias.shape == (E,)
+    w = np.empty((T, topk), np.float32)
+    ids = np.empty((T, topk), np.int32)
+    ties = np.empty((T,), np.uint8)
+    gaps = np.empty((T,), np.float32)
+    scoring = {"softmax": SOFTMAX, "sigmoid": SIGMOID}[scoring_func]
+    rc = lib.oracle_grouped_topk(
+        _ptr(g), dt, T, E, num_expert_group, topk_group, topk, int(bool(renormalize)),
+        float(routed_scaling_factor), _ptr(bias), scoring, exp_mode,
+        _ptr(w), _ptr(ids), _ptr(ties), _ptr(gaps), nthreads,
+    )
+    if rc != 0:
+        raise ValueError(f"oracle_grouped_topk rejected its arguments (code {rc})")
+    return w, ids, ties.astype(bool), gaps
+
+
+def silu_and_mul_bf16(x_bits: np.ndarray, exp_mode: int = EXP_GLIBC, nthreads: int = 0) -> np.ndarray:
+    """x_bits: uint16 [T, 2d] bf16 bits -> uint16 [T, d]."""
+    lib = _load()
+    x = np.ascontiguousarray(x_bits, dtype=np.uint16)
+    T, two_d = x.shape
+    d = two_d // 2
+    out = np.empty((T, d), np.uint16)
+    rc = lib.oracle_silu_and_mul_bf16(_ptr(x), T, d, _ptr(out), exp_mode, nthreads)
+    assert rc == 0
+    return out
+
+
+def rms_norm_bf16(x_bits: np.ndarray, w_bits: np.ndarray, eps: float, nthreads: int = 0) -> np.ndarray:
+    lib = _load()
+    x = np.ascontiguousarray(x_bits, dtype=np.uint16)
+    w = np.ascontiguousarray(w_bits, dtype=np.uint16)
+    T, H = x.shape
+    out = np.empty((T, H), np.uint16)
+    rc = lib.oracle_rms_norm_bf16(_ptr(x), _ptr(w), T, H, float(eps), _ptr(out), nthreads)
+    assert rc == 0
+    return out
+
+
+def sigmoid_f32(x: np.ndarray, exp_mode: int = EXP_GLIBC) -> np.ndarray:
+    lib = _load()
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty_like(x)
+    lib.oracle_sigmoid_f32(_ptr(x), x.size, _ptr(out), exp_mode)
+    return out
+
+
+# ---------------------------------------------------------------- bf16 helpers
+def bf16_bits_to_f32(bits: np.ndarray) -> np.ndarray:
+    return (np.asarray(bits, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
+    """Round-to-nearest-even, as c10::BFloat16 does for finite values."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    lsb = (u >> 16) & 1
+    r = ((u + 0x7FFF + lsb) >> 16).astype(np.uint16)
+    nan = np.isnan(np.asarray(x, dtype=np.float32))
+    if nan.any():
+        r[nan] = 0x7FC0
+    return r
+
+
+# ---------------------------------------------------------------- MLP
+def gemm_bf16(a_bits: np.ndarray, w_bits: np.ndarray) -> np.ndarray:
+    """C = A @ W^T with bf16 operands, fp64 accumulation, bf16 result
+    (csrc/aten/ops/mm.cpp:13-43 runs at::mm_out on CPU: bf16 in, fp32
+    accumulation, bf16 out)."""
+    a = bf16_bits_to_f32(a_bits).astype(np.float64)
+    w = bf16_bits_to_f32(w_bits).astype(np.float64)
+    return f32_to_bf16_bits((a @ w.T).astype(np.float32))
+
+
+def tp_mlp_bf16(
+    x_bits: np.ndarray,
+    w_gate_up_shards: list[np.ndarray],
+    w_down_shards: list[np.ndarray],
+    rms_weight_bits: np.ndarray | None = None,
+    eps: float = 1e-6,
+    exp_mode: int = EXP_GLIBC,
+) -> np.ndarray:
+    """Tensor-parallel gated MLP, one shard per rank, then the SUM all-reduce
+    (example/01_mlp_tp4/run.py:50-56 forward, 106-113 step).
+
+    Each rank: h = x (optionally rms_norm'd) ; gu = h @ Wgu_r^T (bf16) ;
+    a = silu(gu[:, :I_r]) * gu[:, I_r:] (bf16) ; y_r = a @ Wd_r^T (bf16).
+    Output: bf16(sum_r y_r) with the sum in fp32.
+    """
+    h = x_bits
+    if rms_weight_bits is not None:
+        h = rms_norm_bf16(x_bits, rms_weight_bits, eps)
+    acc = None
+    for wgu, wd in zip(w_gate_up_shards, w_down_shards):
+        gu = gemm_bf16(h, wgu)
+        a = silu_and_mul_bf16(gu, exp_mode)
+        y = bf16_bits_to_f32(gemm_bf16(a, wd))
+        acc = y if acc is None else acc + y
+    return f32_to_bf16_bits(acc)
