@@ -1,0 +1,419 @@
+"""Benchmark of the mcpu device hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (one "step"): the DeepSeek-V3-style grouped_topk router over one
+batch of 65536 tokens x 256 experts (fp32 logits N(0,1), fp32 bias N(0,0.01),
+8 groups, top-4 groups, top-8, sigmoid + bias, renormalised, x2.5).  Inputs
+rotate through 8 device buffers (8 x 67 MB > 2 x L2) so no step reads its
+logits from L2.  Steps are replayed from a CUDA graph of the C-ABI launches;
+W warm-up steps, then K timed steps between barriers and device syncs,
+timed with CUDA events on the launching stream, max over ranks.
+
+Multi-GPU: the router is independent per token, so N ranks run N replicas
+(weak scaling, no collective on the data path); `value` is all ranks'
+tokens over the slowest rank's time.
+
+--impl reference times the reference algorithm on the host cores (the
+oracle's C restatement of the reference's CPU path, all threads), rank 0
+only, on the same configuration.
+
+Prints one JSON line (rank 0).
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import re
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
+
+METRIC = "grouped_topk Mtok/s + HBM GB/s; TP-MLP TFLOP/s at 1/2/4/8 B200 vs CPU"
+T, E, G, TG, K = 65536, 256, 8, 4, 8
+BYTES_PER_TOKEN = E * 4 + K * 4 + K * 4  # logits in, weights + ids out
+N_BUFFERS = 8
+GRAPH_STEPS = 64
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=64)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0,
+                    help="bound on the host-core baseline's sampling time")
+    return ap.parse_args()
+
+
+def workload_config(n):
+    return {
+        "workload": f"grouped_topk T={T} E={E} G={G} topk_group={TG} topk={K} sigmoid+bias "
+                    "renormalize x2.5 (DeepSeek-V3 router)",
+        "tokens_per_step_per_gpu": T,
+        "global_batch": T * n,
+        "l2": f"inputs rotate over {N_BUFFERS} device buffers of {T * E * 4 / 1e6:.1f} MB "
+              "(> 2 x L2), no L2 flush needed",
+        "parallelism": f"replicas x{n}",
+    }
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def profiled_traffic(name: str):
+    """DRAM bytes per launch recorded from an ncu capture in profiles/."""
+    path = os.path.join(ROOT, "profiles", name)
+    try:
+        txt = open(path).read()
+    except OSError:
+        return None
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", txt)
+    return float(m.group(1)) if m else None
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML while running."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+        0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+        0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+    }
+
+    def __init__(self, index: int):
+        self.index = index
+        self.samples = []
+        self.reasons = 0
+        self._stop = threading.Event()
+        self._t = None
+        self.max_mhz = None
+
+    def __enter__(self):
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._nv = None
+            return self
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        return self
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                try:
+                    r = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                except AttributeError:
+                    r = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self._h)
+                self.reasons |= int(r) & ~0x1
+            except Exception:
+                pass
+            time.sleep(0.005)
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._t:
+            self._t.join()
+
+    def summary(self):
+        return {
+            "sm_mhz": statistics.median(self.samples) if self.samples else None,
+            "sm_max_mhz": self.max_mhz,
+            "samples": len(self.samples),
+            "reasons": [n for b, n in self.REASONS.items() if self.reasons & b],
+            "source": "nvml, 5 ms polling during the timed region",
+        }
+
+
+# ---------------------------------------------------------------- CPU leg
+def cpu_baseline(seconds: float):
+    """The reference algorithm on the host cores: the oracle's C restatement
+    of the reference's CPU path (kind "port"), all host threads."""
+    import numpy as np
+
+    import configs as C
+    import oracle
+
+    cfg = C.deepseek_v3(T)
+    gating, bias = C.router_inputs(cfg)
+    g, b = gating.numpy(), bias.numpy()
+    threads = os.cpu_count() or 1
+    oracle.grouped_topk(g[:1024], K, True, G, TG, "sigmoid", 2.5, b, nthreads=threads)
+    times = []
+    t_end = time.perf_counter() + seconds
+    while True:
+        t0 = time.perf_counter()
+        oracle.grouped_topk(g, K, True, G, TG, "sigmoid", 2.5, b, nthreads=threads)
+        times.append(time.perf_counter() - t0)
+        if time.perf_counter() > t_end or len(times) >= 200:
+            break
+    med = statistics.median(times)
+    return {
+        "value": round(T / med / 1e6, 4),
+        "unit": "Mtok/s",
+        "cores": threads,
+        "kind": "port",
+        "sample": f"{len(times)} runs of the full {T}x{E} batch (median {med * 1e3:.1f} ms), "
+                  f"oracle C restatement with glibc expf, {threads} OpenMP threads",
+    }
+
+
+# ---------------------------------------------------------------- dist
+def dist_setup(n):
+    import torch
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n:
+        raise SystemExit(f"--gpus {n} but WORLD_SIZE={world}")
+    pg = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+        pg = dist
+    return rank, world, local, pg
+
+
+def barrier(pg):
+    if pg is not None:
+        pg.barrier()
+
+
+def max_over_ranks(pg, v: float, dev) -> float:
+    if pg is None:
+        return v
+    import torch
+
+    t = torch.tensor([v], dtype=torch.float64, device=dev)
+    pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------- ours
+def run_ours(a):
+    import numpy as np
+    import torch
+
+    import configs as C
+    from torch_mcpu_b200 import _lib
+
+    rank, world, local, pg = dist_setup(a.gpus)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    lib = _lib.load()
+
+    cfg = C.deepseek_v3(T)
+    gating_cpu, bias_cpu = C.router_inputs(cfg)
+    bufs = [gating_cpu.to(dev)]
+    for i in range(1, N_BUFFERS):  # distinct contents, same distribution
+        g = torch.Generator(device=dev).manual_seed(100 + i)
+        bufs.append(torch.randn(T, E, generator=g, device=dev))
+    bias = bias_cpu.to(dev)
+    w = torch.empty(T, K, dtype=torch.float32, device=dev)
+    ids = torch.empty(T, K, dtype=torch.int32, device=dev)
+    stream = torch.cuda.Stream(dev)
+
+    def launch(i):
+        rc = lib.mcpu_grouped_topk(bufs[i % N_BUFFERS].data_ptr(), 0, T, E, G, TG, K, 1, 2.5,
+                                   bias.data_ptr(), 1, w.data_ptr(), ids.data_ptr(),
+                                   stream.cuda_stream)
+        if rc != 0:
+            _lib.check(rc, "grouped_topk")
+
+    # correctness spot check of this exact configuration before timing
+    with torch.cuda.stream(stream):
+        launch(0)
+    stream.synchronize()
+    if rank == 0:
+        import oracle
+
+        ow, oids, _, _ = oracle.grouped_topk(gating_cpu[:4096].numpy(), K, True, G, TG, "sigmoid",
+                                             2.5, bias_cpu.numpy(), exp_mode=oracle.EXP_CR)
+        got = np.sort(ids[:4096].cpu().numpy(), 1)
+        if not np.array_equal(got, np.sort(oids, 1)):
+            raise SystemExit("bench: router output differs from the oracle; refusing to time it")
+
+    # CUDA graph of GRAPH_STEPS launches (rotating buffers)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        for i in range(3):
+            launch(i)
+    stream.synchronize()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(GRAPH_STEPS):
+            launch(i)
+    reps_w = max(1, -(-a.warmup // GRAPH_STEPS))
+    reps = max(1, -(-a.steps // GRAPH_STEPS))
+    steps = reps * GRAPH_STEPS
+
+    exact_before = ctypes.c_ulonglong(0)
+    lib.mcpu_grouped_topk_exact_rows(ctypes.byref(exact_before), 1)
+    with torch.cuda.stream(stream):
+        for _ in range(reps_w):
+            graph.replay()
+    stream.synchronize()
+    barrier(pg)
+    torch.cuda.synchronize(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+            for _ in range(reps):
+                graph.replay()
+            ev1.record(stream)
+        ev1.synchronize()
+    torch.cuda.synchronize(dev)
+    barrier(pg)
+    ms = ev0.elapsed_time(ev1)
+    ms_max = max_over_ranks(pg, ms, dev)
+    exact = ctypes.c_ulonglong(0)
+    lib.mcpu_grouped_topk_exact_rows(ctypes.byref(exact), 0)
+    exact_per_step = exact.value / (steps + reps_w * GRAPH_STEPS)
+
+    # e2e through the C-ABI with host buffers: H2D logits, kernel, D2H results
+    host_in = torch.empty(T, E, dtype=torch.float32, pin_memory=True)
+    host_in.copy_(gating_cpu)
+    host_w = torch.empty(T, K, dtype=torch.float32, pin_memory=True)
+    host_ids = torch.empty(T, K, dtype=torch.int32, pin_memory=True)
+    dbuf = bufs[0]
+    h2d = T * E * 4
+    d2h = T * K * 8
+    s_handle = stream.cuda_stream
+
+    def e2e_step():
+        _lib.check(lib.orMemcpyAsync(dbuf.data_ptr(), host_in.data_ptr(), h2d, 1, s_handle), "H2D")
+        _lib.check(lib.mcpu_grouped_topk(dbuf.data_ptr(), 0, T, E, G, TG, K, 1, 2.5,
+                                         bias.data_ptr(), 1, w.data_ptr(), ids.data_ptr(),
+                                         s_handle), "grouped_topk")
+        _lib.check(lib.orMemcpyAsync(host_w.data_ptr(), w.data_ptr(), T * K * 4, 2, s_handle), "D2H")
+        _lib.check(lib.orMemcpyAsync(host_ids.data_ptr(), ids.data_ptr(), T * K * 4, 2, s_handle), "D2H")
+
+    e2e_steps = max(3, min(a.steps, 200))
+    for _ in range(3):
+        e2e_step()
+    stream.synchronize()
+    barrier(pg)
+    with torch.cuda.stream(stream):
+        ev0.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        ev1.record(stream)
+    ev1.synchronize()
+    barrier(pg)
+    e2e_ms = max_over_ranks(pg, ev0.elapsed_time(ev1), dev) / e2e_steps
+
+    if rank == 0:
+        per_step = ms_max / steps
+        peak, peak_kind = measured_peaks()
+        achieved = BYTES_PER_TOKEN * T / (per_step * 1e-3) / 1e9
+        traffic = profiled_traffic("grouped_topk_T65536_E256.md")
+        line = {
+            "metric": METRIC,
+            "value": round(T * world / (per_step * 1e-3) / 1e6, 2),
+            "unit": "Mtok/s",
+            "n_gpus": world,
+            "steps": steps,
+            "warmup": reps_w * GRAPH_STEPS,
+            "ms_per_step": round(per_step, 6),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f32",
+            "data": "synthetic (seeded N(0,1) logits, N(0,0.01) bias)",
+            "config": workload_config(world),
+            "roofline": {
+                "bound": "hbm",
+                "achieved": round(achieved, 1),
+                "peak": peak,
+                "unit": "GB/s",
+                "frac": round(achieved / peak, 4),
+                "peak_kind": peak_kind,
+                "traffic": traffic,
+                "algorithmic_bytes_per_launch": BYTES_PER_TOKEN * T,
+            },
+            "e2e": {
+                "value": round(T * world / (e2e_ms * 1e-3) / 1e6, 2),
+                "unit": "Mtok/s",
+                "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h,
+                "path": "orMemcpyAsync H2D (pinned) -> mcpu_grouped_topk -> orMemcpyAsync D2H",
+            },
+            "clocks": clk.summary(),
+            "gpu_launches": steps,
+            "exact_path_rows_per_step": round(exact_per_step, 2),
+        }
+        line["cpu_baseline"] = cpu_baseline(a.cpu_seconds) if world == 1 else None
+        print(json.dumps(line), flush=True)
+    del graph
+    if pg is not None:
+        pg.destroy_process_group()
+
+
+def run_reference(a):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    base = cpu_baseline(a.cpu_seconds)
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": base["value"],
+        "unit": "Mtok/s",
+        "n_gpus": world,
+        "steps": a.steps,
+        "warmup": a.warmup,
+        "ms_per_step": round(T / (base["value"] * 1e6) * 1e3, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded N(0,1) logits, N(0,0.01) bias)",
+        "config": workload_config(1),
+        "cpu_baseline": base,
+        "e2e": {"value": base["value"], "unit": "Mtok/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    a = parse()
+    if a.impl == "reference":
+        run_reference(a)
+    else:
+        run_ours(a)
+
+
+if __name__ == "__main__":
+    main()

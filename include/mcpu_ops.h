@@ -1,0 +1,106 @@
+/*
+ * Hot-path op entry points of the mcpu device on B200 (sm_100a): a C-ABI of
+ * plain pointers, sizes and a stream.  Every pointer named "device" is HBM
+ * (orMalloc / cudaMalloc / a torch CUDA tensor's data_ptr); every call is
+ * asynchronous on `stream` like the reference's ops, which return after
+ * enqueueing on the current mcpu stream (docs/kernel_launch_migration.md,
+ * "Migration checkpoints").
+ *
+ * Error behaviour: argument problems return orErrorInvalidValue and launch
+ * failures orErrorUnknown, with the message in mcpuGetLastErrorString();
+ * the Python layer raises RuntimeError with it, where the reference raises
+ * c10::Error from TORCH_CHECK.  There is no CPU fallback: with no usable
+ * device the call fails.
+ */
+#pragma once
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "openreg.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum mcpuDtype {
+  MCPU_FLOAT32 = 0,
+  MCPU_BFLOAT16 = 1
+} mcpuDtype;
+
+typedef enum mcpuScoring {
+  MCPU_SCORING_SOFTMAX = 0,
+  MCPU_SCORING_SIGMOID = 1
+} mcpuScoring;
+
+/* Text of the last error raised on this host thread ("" if none). */
+OPENREG_EXPORT const char* mcpuGetLastErrorString(void);
+
+/*
+ * Grouped top-k MoE router, one fused kernel.
+ *
+ * Replaces the aten chain of copied_grouped_topk
+ * (tests/test_grouped_topk_compile.py:15-66), which on the reference runs as
+ * sigmoid (csrc/aten/ops/unary_out.cpp:415-430) or _softmax
+ * (csrc/aten/ops/softmax_random_argmax.cpp:57-82), add
+ * (binary_out.cpp:259), three topk (topk.cpp:10-40), sum/max
+ * (reduction_scatter.cpp:116-150, 461-495), the scatter/masked_fill mask
+ * (unary_out.cpp:684-700; scatter.value_out falls back to CPU), gather
+ * (gather.cpp:10-31), div and mul (binary_out.cpp:307, 544).
+ *
+ * gating        device, [num_tokens, num_experts] row-major, fp32 or bf16
+ * bias          device fp32 [num_experts] or NULL (e_score_correction_bias)
+ * topk_weights  device fp32 [num_tokens, topk]
+ * topk_ids      device int32 [num_tokens, topk]
+ *
+ * Constraints: num_experts % num_expert_group == 0, num_expert_group a power
+ * of two <= 32, group size <= 64 (>= 2 with a bias), topk <= 16,
+ * topk <= topk_group * group size, num_experts <= 1024.
+ *
+ * Semantics: experts are ranked by the biased score (score + bias) when a
+ * bias is given, else by the logit (order-equivalent to softmax/sigmoid);
+ * ties go to the lower index (group or expert).  Outputs are ordered by rank.
+ * Sigmoid scores equal 1/(1 + e^-x) with e^-x correctly rounded to fp32.
+ */
+OPENREG_EXPORT orError_t mcpu_grouped_topk(
+    const void* gating, int gating_dtype, int64_t num_tokens, int num_experts,
+    int num_expert_group, int topk_group, int topk, int renormalize,
+    float routed_scaling_factor, const float* bias, int scoring_func,
+    float* topk_weights, int32_t* topk_ids, orStream_t stream);
+
+/* Number of rows the router resolved on its exact (near-tie) path since the
+ * last reset, summed over all launches on the current device. */
+OPENREG_EXPORT orError_t mcpu_grouped_topk_exact_rows(
+    unsigned long long* count, int reset);
+
+/*
+ * silu_and_mul: out[t, j] = silu(x[t, j]) * x[t, d + j] for x [T, 2d],
+ * out [T, d], both contiguous bf16 on the device.
+ *
+ * Replaces vLLM's SiluAndMul.forward_native
+ * (vllm/model_executor/layers/activation.py:135-139) as the reference runs
+ * it: the raw silu loop x / (1.0f + std::exp(-x)) rounded to bf16
+ * (csrc/aten/ops/unary_out.cpp:50-51, silu_out 456-470), then aten mul
+ * (csrc/aten/ops/binary_out.cpp:544-560) rounded to bf16.  Schema of the
+ * matching custom op: mcpu::silu_and_mul(Tensor(a!) out, Tensor x) -> ().
+ */
+OPENREG_EXPORT orError_t mcpu_silu_and_mul(void* out, const void* x, int64_t num_tokens,
+                                           int64_t d, int dtype, orStream_t stream);
+
+/*
+ * rms_norm: out = bf16(bf16(x * rsqrt(mean(x^2) + eps)) * weight) per row of
+ * x [T, H] (bf16), weight [H] (bf16), out [T, H] (bf16).
+ *
+ * Replaces vLLM's rms_norm native implementation
+ * (vllm/ir/ops/layernorm.py:14-21), which the reference runs as pow and
+ * rsqrt (CPU fallback), mean (csrc/aten/ops/reduction_scatter.cpp:248-285),
+ * add and mul (binary_out.cpp).  Schema of the matching custom op:
+ * mcpu::rms_norm(Tensor(a!) out, Tensor x, Tensor weight, float eps) -> ().
+ */
+OPENREG_EXPORT orError_t mcpu_rms_norm(void* out, const void* x, const void* weight,
+                                       int64_t num_tokens, int64_t hidden, float eps,
+                                       int dtype, orStream_t stream);
+
+#ifdef __cplusplus
+}  // extern "C"
+#endif

@@ -1,0 +1,73 @@
+"""The C-ABI library loads and exports every entry point include/*.h declares.
+
+CPU only: nothing here launches device work.
+"""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    names = []
+    for h in sorted(os.listdir(os.path.join(ROOT, "include"))):
+        if not h.endswith(".h"):
+            continue
+        src = open(os.path.join(ROOT, "include", h)).read()
+        src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+        src = "\n".join(line for line in src.splitlines() if not line.lstrip().startswith("#"))
+        for m in re.finditer(r"OPENREG_EXPORT\s+[^;(]*?\b(\w+)\s*\(", src):
+            names.append(m.group(1))
+    return names
+
+
+def test_headers_declare_entry_points():
+    names = declared_symbols()
+    assert "orMalloc" in names and "mcpu_grouped_topk" in names
+    assert len(names) == len(set(names))
+
+
+def test_library_exports_every_declared_symbol():
+    from torch_mcpu_b200 import _lib
+
+    lib = _lib.load()
+    missing = [n for n in declared_symbols() if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_python_signatures_cover_every_declared_symbol():
+    from torch_mcpu_b200 import _lib
+
+    assert set(declared_symbols()) <= set(_lib.SIGNATURES)
+
+
+def test_error_string_and_argument_validation_without_device():
+    """Argument checks run on the host before any device call."""
+    from torch_mcpu_b200 import _lib
+
+    lib = _lib.load()
+    rc = lib.mcpu_grouped_topk(None, 0, 4, 12, 8, 1, 2, 1, 1.0, None, 0, None, None, None)
+    assert rc == 4  # orErrorInvalidValue
+    assert b"divisible" in lib.mcpuGetLastErrorString()
+    rc = lib.mcpu_grouped_topk(None, 0, 0, 256, 8, 4, 8, 1, 1.0, None, 1, None, None, None)
+    assert rc == 0  # zero tokens: nothing to do
+
+
+def test_priority_range_matches_reference_convention():
+    from torch_mcpu_b200 import _lib
+
+    lib = _lib.load()
+    lo, hi = ctypes.c_int(-9), ctypes.c_int(-9)
+    assert lib.orDeviceGetStreamPriorityRange(ctypes.byref(lo), ctypes.byref(hi)) == 0
+    assert (lo.value, hi.value) == (1, 0)
+
+
+def test_memory_protection_calls_are_accepted():
+    from torch_mcpu_b200 import _lib
+
+    lib = _lib.load()
+    assert lib.orMemoryProtect(None) == 0 and lib.orMemoryUnprotect(None) == 0

@@ -1,0 +1,92 @@
+"""ctypes view of libtorch_mcpu_b200.so (the C-ABI in include/*.h).
+
+The library is built in-tree (torch_mcpu_b200/build.py).  Loading fails
+loudly when it is missing: there is no CPU fallback for any op.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+
+from . import build as _build
+
+_lib = None
+
+c_int, c_int64, c_float, c_void_p = ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p
+
+# name -> (restype, argtypes); every entry point declared in include/*.h
+SIGNATURES = {
+    # include/openreg.h
+    "orMalloc": (c_int, [ctypes.POINTER(c_void_p), ctypes.c_size_t]),
+    "orFree": (c_int, [c_void_p]),
+    "orMallocHost": (c_int, [ctypes.POINTER(c_void_p), ctypes.c_size_t]),
+    "orFreeHost": (c_int, [c_void_p]),
+    "orMemcpy": (c_int, [c_void_p, c_void_p, ctypes.c_size_t, c_int]),
+    "orMemcpyAsync": (c_int, [c_void_p, c_void_p, ctypes.c_size_t, c_int, c_void_p]),
+    "orPointerGetAttributes": (c_int, [c_void_p, c_void_p]),
+    "orMemoryUnprotect": (c_int, [c_void_p]),
+    "orMemoryProtect": (c_int, [c_void_p]),
+    "orGetDeviceCount": (c_int, [ctypes.POINTER(c_int)]),
+    "orSetDevice": (c_int, [c_int]),
+    "orGetDevice": (c_int, [ctypes.POINTER(c_int)]),
+    "orDeviceGetStreamPriorityRange": (c_int, [ctypes.POINTER(c_int), ctypes.POINTER(c_int)]),
+    "orDeviceSynchronize": (c_int, []),
+    "orStreamCreateWithPriority": (c_int, [ctypes.POINTER(c_void_p), ctypes.c_uint, c_int]),
+    "orStreamCreate": (c_int, [ctypes.POINTER(c_void_p)]),
+    "orStreamGetPriority": (c_int, [c_void_p, ctypes.POINTER(c_int)]),
+    "orStreamDestroy": (c_int, [c_void_p]),
+    "orStreamQuery": (c_int, [c_void_p]),
+    "orStreamSynchronize": (c_int, [c_void_p]),
+    "orStreamWaitEvent": (c_int, [c_void_p, c_void_p, ctypes.c_uint]),
+    "orEventCreateWithFlags": (c_int, [ctypes.POINTER(c_void_p), ctypes.c_uint]),
+    "orEventCreate": (c_int, [ctypes.POINTER(c_void_p)]),
+    "orEventDestroy": (c_int, [c_void_p]),
+    "orEventRecord": (c_int, [c_void_p, c_void_p]),
+    "orEventSynchronize": (c_int, [c_void_p]),
+    "orEventQuery": (c_int, [c_void_p]),
+    "orEventElapsedTime": (c_int, [ctypes.POINTER(c_float), c_void_p, c_void_p]),
+    # include/mcpu_ops.h
+    "mcpuGetLastErrorString": (ctypes.c_char_p, []),
+    "mcpu_grouped_topk": (c_int, [c_void_p, c_int, c_int64, c_int, c_int, c_int, c_int, c_int,
+                                  c_float, c_void_p, c_int, c_void_p, c_void_p, c_void_p]),
+    "mcpu_grouped_topk_exact_rows": (c_int, [ctypes.POINTER(ctypes.c_ulonglong), c_int]),
+    "mcpu_silu_and_mul": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int, c_void_p]),
+    "mcpu_rms_norm": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_float, c_int, c_void_p]),
+}
+
+
+def lib_path() -> str:
+    return _build.LIB
+
+
+def load(build_if_missing: bool = True):
+    """Load the device library, building it first when it is missing (or,
+    with MCPU_AUTOBUILD=1, older than its sources)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    path = _build.LIB
+    stale = os.environ.get("MCPU_AUTOBUILD") == "1" and not _build.up_to_date()
+    if build_if_missing and (not os.path.exists(path) or stale):
+        _build.build()
+    if not os.path.exists(path):
+        raise RuntimeError(f"mcpu device library not built: {path} is missing "
+                           "(run python -m torch_mcpu_b200.build)")
+    lib = ctypes.CDLL(path)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+ERROR_NAMES = {0: "orSuccess", 1: "orErrorUnknown", 2: "orErrorNotReady", 3: "orErrorTimeout",
+               4: "orErrorInvalidValue"}
+
+
+def check(rc: int, what: str) -> None:
+    if rc != 0:
+        msg = load().mcpuGetLastErrorString().decode(errors="replace")
+        raise RuntimeError(f"{what} failed ({ERROR_NAMES.get(rc, rc)}): {msg}")

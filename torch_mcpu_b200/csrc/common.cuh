@@ -1,0 +1,50 @@
+// Shared helpers for the sm_100a kernels and the C-ABI layer.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "openreg.h"
+#include "mcpu_ops.h"
+
+namespace mcpu {
+
+// Thread-local last-error text behind mcpuGetLastErrorString().
+void set_last_error(const char* fmt, ...);
+
+// Maps a CUDA status to orError_t, recording the CUDA message on failure.
+orError_t from_cuda(cudaError_t st, const char* what);
+
+inline cudaStream_t as_cuda(orStream_t s) {
+  return reinterpret_cast<cudaStream_t>(s);
+}
+
+#define MCPU_CUDA_TRY(expr, what)                         \
+  do {                                                    \
+    cudaError_t _st = (expr);                             \
+    if (_st != cudaSuccess) return ::mcpu::from_cuda(_st, what); \
+  } while (0)
+
+#define MCPU_ARG_CHECK(cond, ...)                         \
+  do {                                                    \
+    if (!(cond)) {                                        \
+      ::mcpu::set_last_error(__VA_ARGS__);                \
+      return orErrorInvalidValue;                         \
+    }                                                     \
+  } while (0)
+
+__device__ __forceinline__ float bf16_bits_to_float(uint16_t h) {
+  return __uint_as_float(static_cast<uint32_t>(h) << 16);
+}
+
+// Round-to-nearest-even fp32 -> bf16 bits (finite values; NaN kept quiet).
+__device__ __forceinline__ uint16_t float_to_bf16_bits(float f) {
+  return __bfloat16_as_ushort(__float2bfloat16_rn(f));
+}
+
+__device__ __forceinline__ float round_bf16(float f) {
+  return bf16_bits_to_float(float_to_bf16_bits(f));
+}
+
+}  // namespace mcpu

@@ -1,0 +1,114 @@
+"""Python surface of the hot-path ops, mirroring the reference's interface.
+
+Tensors are torch tensors resident on the B200 (device "cuda"); every op is
+enqueued on torch's current CUDA stream and returns without synchronising,
+like the reference's mcpu ops, which return after enqueueing on the current
+mcpu stream.  Each call goes straight to the C-ABI of include/mcpu_ops.h.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+_DTYPES = {torch.float32: 0, torch.bfloat16: 1}
+_SCORING = {"softmax": 0, "sigmoid": 1}
+
+
+def _stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _require_device(t: torch.Tensor, name: str) -> None:
+    if not t.is_cuda:
+        raise RuntimeError(f"{name} must be a device tensor (got device {t.device}); "
+                           "the mcpu B200 ops have no CPU fallback")
+
+
+def grouped_topk(
+    hidden_states: torch.Tensor,
+    gating_output: torch.Tensor,
+    topk: int,
+    renormalize: bool,
+    num_expert_group: int,
+    topk_group: int,
+    scoring_func: str = "softmax",
+    routed_scaling_factor: float = 1.0,
+    e_score_correction_bias: torch.Tensor | None = None,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Fused grouped top-k router; same arguments and outputs as the
+    reference's copied_grouped_topk (tests/test_grouped_topk_compile.py:15-26):
+    returns (topk_weights float32 [T, topk], topk_ids int32 [T, topk])."""
+    if hidden_states.size(0) != gating_output.size(0):
+        raise AssertionError("Number of tokens mismatch")
+    if scoring_func not in _SCORING:
+        raise ValueError(f"Unsupported scoring function: {scoring_func}")
+    _require_device(gating_output, "gating_output")
+    if gating_output.dim() != 2:
+        raise RuntimeError("grouped_topk: gating_output must be [num_tokens, num_experts]")
+    if gating_output.dtype not in _DTYPES:
+        raise RuntimeError(f"grouped_topk: unsupported gating dtype {gating_output.dtype}")
+    g = gating_output.contiguous()
+    T, E = g.shape
+    bias = None
+    if e_score_correction_bias is not None:
+        _require_device(e_score_correction_bias, "e_score_correction_bias")
+        if e_score_correction_bias.numel() != E:
+            raise RuntimeError("grouped_topk: e_score_correction_bias must have num_experts elements")
+        bias = e_score_correction_bias.to(torch.float32).contiguous()
+    w = torch.empty(T, topk, dtype=torch.float32, device=g.device)
+    ids = torch.empty(T, topk, dtype=torch.int32, device=g.device)
+    lib = _lib.load()
+    rc = lib.mcpu_grouped_topk(
+        g.data_ptr(), _DTYPES[g.dtype], T, E, num_expert_group, topk_group, topk,
+        int(bool(renormalize)), float(routed_scaling_factor),
+        None if bias is None else bias.data_ptr(), _SCORING[scoring_func],
+        w.data_ptr(), ids.data_ptr(), _stream_handle(g.device),
+    )
+    _lib.check(rc, "grouped_topk")
+    return w, ids
+
+
+def grouped_topk_exact_rows(reset: bool = False) -> int:
+    """Rows resolved on the router's exact near-tie path (diagnostics)."""
+    import ctypes
+
+    n = ctypes.c_ulonglong(0)
+    _lib.check(_lib.load().mcpu_grouped_topk_exact_rows(ctypes.byref(n), int(reset)),
+               "grouped_topk_exact_rows")
+    return int(n.value)
+
+
+def silu_and_mul(out: torch.Tensor, x: torch.Tensor) -> None:
+    """mcpu::silu_and_mul(Tensor(a!) out, Tensor x) -> (): out = silu(x[..., :d]) * x[..., d:]
+    (vLLM SiluAndMul, activation.py:118-140), bf16."""
+    _require_device(x, "x")
+    _require_device(out, "out")
+    d = x.shape[-1] // 2
+    if x.shape[-1] != 2 * d or tuple(out.shape) != tuple(x.shape[:-1]) + (d,):
+        raise RuntimeError(f"silu_and_mul: out must be {tuple(x.shape[:-1]) + (d,)}, got {tuple(out.shape)}")
+    if x.dtype != torch.bfloat16 or out.dtype != torch.bfloat16:
+        raise RuntimeError("silu_and_mul: bfloat16 tensors expected")
+    if not (x.is_contiguous() and out.is_contiguous()):
+        raise RuntimeError("silu_and_mul: contiguous tensors expected")
+    T = x.numel() // max(1, x.shape[-1])
+    _lib.check(_lib.load().mcpu_silu_and_mul(out.data_ptr(), x.data_ptr(), T, d, 1,
+                                             _stream_handle(x.device)), "silu_and_mul")
+
+
+def rms_norm(out: torch.Tensor, x: torch.Tensor, weight: torch.Tensor, eps: float) -> None:
+    """mcpu::rms_norm(Tensor(a!) out, Tensor x, Tensor weight, float eps) -> ()
+    (vLLM rms_norm native, vllm/ir/ops/layernorm.py:10-21), bf16."""
+    for t, n in ((x, "x"), (out, "out"), (weight, "weight")):
+        _require_device(t, n)
+        if t.dtype != torch.bfloat16:
+            raise RuntimeError(f"rms_norm: {n} must be bfloat16")
+        if not t.is_contiguous():
+            raise RuntimeError(f"rms_norm: {n} must be contiguous")
+    H = x.shape[-1]
+    if weight.numel() != H or out.shape != x.shape:
+        raise RuntimeError("rms_norm: shape mismatch")
+    T = x.numel() // H
+    _lib.check(_lib.load().mcpu_rms_norm(out.data_ptr(), x.data_ptr(), weight.data_ptr(), T, H,
+                                         float(eps), 1, _stream_handle(x.device)), "rms_norm")
