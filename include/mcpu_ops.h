@@ -101,6 +101,48 @@ OPENREG_EXPORT orError_t mcpu_rms_norm(void* out, const void* x, const void* wei
                                        int64_t num_tokens, int64_t hidden, float eps,
                                        int dtype, orStream_t stream);
 
+/*
+ * mm: out[M, N] = a[M, K] . b[N, K]^T in bf16 with fp32 accumulation on the
+ * tcgen05 tensor cores (TMA-fed shared-memory tiles, TMEM accumulators).
+ * a, b, out contiguous row-major on the device, 16-byte aligned, K and N
+ * multiples of 8 (the TMA stride rule).  b is the weight as stored by
+ * nn.Linear, so this is torch.mm(a, b.t()).
+ *
+ * Replaces aten::mm / mm.out (csrc/aten/ops/mm.cpp:13-51), which calls
+ * at::mm_out on host views of the operands.
+ */
+OPENREG_EXPORT orError_t mcpu_mm(const void* a, const void* b, void* out, int64_t M, int64_t N,
+                                 int64_t K, int dtype, orStream_t stream);
+
+/*
+ * addmm: out = bf16(a . b^T + bias) with bias [N] bf16 added to the fp32
+ * accumulator (one rounding).  Replaces aten::addmm / addmm.out
+ * (csrc/aten/ops/mm.cpp:53-110).
+ */
+OPENREG_EXPORT orError_t mcpu_addmm(const void* bias, const void* a, const void* b, void* out,
+                                    int64_t M, int64_t N, int64_t K, int dtype,
+                                    orStream_t stream);
+
+/*
+ * gemm_swiglu: the gated MLP's gate/up projection with silu_and_mul fused
+ * into the epilogue: out[M, I] = bf16(bf16(silu(bf16(x.Wg^T))) * bf16(x.Wu^T)),
+ * i.e. exactly mm followed by mcpu_silu_and_mul, without writing the [M, 2I]
+ * intermediate.  w_gate_up [2I, K] holds the gate and up rows interleaved in
+ * blocks of 128: rows [256j, 256j+128) = Wg[128j .. 128j+128),
+ * rows [256j+128, 256j+256) = Wu[128j .. 128j+128); I % 128 == 0.
+ * Replaces the mm -> silu -> mul chain of the reference's TP MLP
+ * (example/01_mlp_tp4/run.py:50-56) in its SwiGLU form.
+ */
+OPENREG_EXPORT orError_t mcpu_gemm_swiglu(const void* x, const void* w_gate_up, void* out,
+                                          int64_t M, int64_t I, int64_t K, int dtype,
+                                          orStream_t stream);
+
+/* *flag = 1 if a kernel on the current device (tensor-core GEMM or TMA-fed
+ * router) gave up on a bounded wait since the last reset; that launch left
+ * its output incomplete.  No counterpart in the reference, whose host
+ * worker threads report hangs through orStreamSynchronize's timeout. */
+OPENREG_EXPORT orError_t mcpu_device_error(int* flag, int reset);
+
 #ifdef __cplusplus
 }  // extern "C"
 #endif

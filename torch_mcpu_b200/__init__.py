@@ -6,6 +6,16 @@ the reference's Python signatures.
 """
 
 from . import _lib  # noqa: F401
-from .ops import grouped_topk, grouped_topk_exact_rows, rms_norm, silu_and_mul  # noqa: F401
+from .ops import (  # noqa: F401
+    device_error,
+    gemm_swiglu,
+    grouped_topk,
+    grouped_topk_exact_rows,
+    interleave_gate_up,
+    mm_nt,
+    rms_norm,
+    silu_and_mul,
+)
 
-__all__ = ["grouped_topk", "grouped_topk_exact_rows", "silu_and_mul", "rms_norm"]
+__all__ = ["grouped_topk", "grouped_topk_exact_rows", "silu_and_mul", "rms_norm", "mm_nt",
+           "gemm_swiglu", "interleave_gate_up", "device_error"]

@@ -53,6 +53,12 @@ SIGNATURES = {
     "mcpu_grouped_topk_exact_rows": (c_int, [ctypes.POINTER(ctypes.c_ulonglong), c_int]),
     "mcpu_silu_and_mul": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int, c_void_p]),
     "mcpu_rms_norm": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_float, c_int, c_void_p]),
+    "mcpu_mm": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int, c_void_p]),
+    "mcpu_addmm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int,
+                           c_void_p]),
+    "mcpu_gemm_swiglu": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int,
+                                 c_void_p]),
+    "mcpu_device_error": (c_int, [ctypes.POINTER(c_int), c_int]),
 }
 
 

@@ -16,6 +16,17 @@ void set_last_error(const char* fmt, ...);
 // Maps a CUDA status to orError_t, recording the CUDA message on failure.
 orError_t from_cuda(cudaError_t st, const char* what);
 
+// Driver entry point by name (cudaGetDriverEntryPoint), or nullptr.
+void* driver_entry(const char* name);
+
+// Device error flags of the kernels with bounded waits (OR-ed, optionally reset).
+namespace gemm {
+orError_t read_error(int* flag, bool reset);
+}
+namespace router {
+orError_t read_error(int* flag, bool reset);
+}
+
 inline cudaStream_t as_cuda(orStream_t s) {
   return reinterpret_cast<cudaStream_t>(s);
 }

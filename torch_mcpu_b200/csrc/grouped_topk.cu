@@ -23,209 +23,17 @@
 // exact computation; any other token (about 0.4% of N(0,1) tokens) is
 // recomputed on the spot with the exact formula and 64-bit keys.  The
 // no-bias and bf16 paths rank on exact keys from the start.
+#include <cuda.h>
 #include <math.h>
+#include <stdlib.h>
 
-#include "common.cuh"
+#include "router_common.cuh"
 
 namespace mcpu {
 namespace router {
 
 __device__ unsigned long long g_exact_rows = 0;
-
-constexpr int kThreads = 256;
-
-__device__ __forceinline__ float ex2_approx(float y) {
-  float r;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(y));
-  return r;
-}
-
-__device__ __forceinline__ float rcp_approx(float y) {
-  float r;
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(y));
-  return r;
-}
-
-// Fast sigmoid used only for ranking; |error| < 2^-21 absolute: the exponent
-// argument carries |x| 2^-24 relative error, ex2.approx about 2^-22, the sum
-// and the approximate reciprocal one rounding each, and s(1-s) <= 1/4 damps
-// the exp error.
-__device__ __forceinline__ float sigmoid_fast(float x) {
-  const float e = ex2_approx(__fmul_rn(x, -1.4426950408889634f));
-  return rcp_approx(__fadd_rn(1.0f, e));
-}
-
-// The reference formula with exp correctly rounded to fp32:
-// (float)exp((double)y) rounds correctly for every fp32 y (checked
-// exhaustively against an extended-precision exp on the host).
-__device__ __forceinline__ float sigmoid_exact(float x) {
-  const float e = static_cast<float>(exp(-static_cast<double>(x)));
-  return __fdiv_rn(1.0f, __fadd_rn(1.0f, e));
-}
-
-__device__ __forceinline__ float fast_key(float x, float b) {
-  return __fadd_rn(sigmoid_fast(x), b);
-}
-
-__device__ __forceinline__ uint32_t orderable(float f) {
-  const uint32_t u = __float_as_uint(f);
-  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
-
-// Keys packed so that an unsigned compare ranks by value, then by lower
-// index.  0 means "no element".
-struct Pack32 {
-  using T = uint32_t;
-  static __device__ __forceinline__ T pack(float f, int idx, uint32_t mask) {
-    return (orderable(f) & ~mask) | (mask - static_cast<uint32_t>(idx));
-  }
-  static __device__ __forceinline__ int index(T k, uint32_t mask) {
-    return static_cast<int>(mask - (k & mask));
-  }
-};
-
-struct Pack64 {
-  using T = unsigned long long;
-  static __device__ __forceinline__ T pack(float f, int idx, uint32_t) {
-    return (static_cast<T>(orderable(f)) << 32) |
-           static_cast<T>(0xFFFFFFFFu - static_cast<uint32_t>(idx));
-  }
-  static __device__ __forceinline__ int index(T k, uint32_t) {
-    return static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(k));
-  }
-};
-
-template <typename K>
-__device__ __forceinline__ K kmax(K a, K b) { return a > b ? a : b; }
-template <typename K>
-__device__ __forceinline__ K kmin(K a, K b) { return a > b ? b : a; }
-
-template <typename K, int N>
-__device__ __forceinline__ void bitonic_sort_desc(K (&a)[N]) {
-#pragma unroll
-  for (int k = 2; k <= N; k <<= 1) {
-#pragma unroll
-    for (int j = k >> 1; j > 0; j >>= 1) {
-#pragma unroll
-      for (int i = 0; i < N; ++i) {
-        const int l = i ^ j;
-        if (l > i) {
-          const K x = a[i], y = a[l];
-          const K hi = kmax(x, y), lo = kmin(x, y);
-          if ((i & k) == 0) {
-            a[i] = hi;
-            a[l] = lo;
-          } else {
-            a[i] = lo;
-            a[l] = hi;
-          }
-        }
-      }
-    }
-  }
-}
-
-template <typename K, int N>
-__device__ __forceinline__ void bitonic_merge_desc(K (&a)[N]) {
-#pragma unroll
-  for (int j = N >> 1; j > 0; j >>= 1) {
-#pragma unroll
-    for (int i = 0; i < N; ++i) {
-      const int l = i ^ j;
-      if (l > i) {
-        const K x = a[i], y = a[l];
-        a[i] = kmax(x, y);
-        a[l] = kmin(x, y);
-      }
-    }
-  }
-}
-
-// best = the L largest of pk[0..GS_MAX), sorted descending.
-template <typename K, int L, int GS_MAX>
-__device__ __forceinline__ void local_top(const K (&pk)[GS_MAX], K (&best)[L]) {
-  if constexpr (GS_MAX <= L) {
-#pragma unroll
-    for (int i = 0; i < L; ++i) best[i] = i < GS_MAX ? pk[i] : K(0);
-    bitonic_sort_desc(best);
-  } else {
-#pragma unroll
-    for (int i = 0; i < L; ++i) best[i] = pk[i];
-    bitonic_sort_desc(best);
-#pragma unroll
-    for (int c = 1; c < GS_MAX / L; ++c) {
-      K t[L];
-#pragma unroll
-      for (int i = 0; i < L; ++i) t[i] = pk[c * L + i];
-      bitonic_sort_desc(t);
-#pragma unroll
-      for (int i = 0; i < L; ++i) best[i] = kmax(best[i], t[L - 1 - i]);
-      bitonic_merge_desc(best);
-    }
-  }
-}
-
-// Butterfly all-merge of the sorted top-L lists of the G lanes of a segment.
-template <typename K, int L>
-__device__ __forceinline__ void segment_merge(K (&best)[L], unsigned segmask, int G) {
-  for (int off = 1; off < G; off <<= 1) {
-    K o[L];
-#pragma unroll
-    for (int i = 0; i < L; ++i) o[i] = __shfl_xor_sync(segmask, best[i], off, G);
-#pragma unroll
-    for (int i = 0; i < L; ++i) best[i] = kmax(best[i], o[L - 1 - i]);
-    bitonic_merge_desc(best);
-  }
-}
-
-template <typename K, int L>
-__device__ __forceinline__ K select_at(const K (&a)[L], int i) {
-  K r = 0;
-#pragma unroll
-  for (int j = 0; j < L; ++j) r = (j == i) ? a[j] : r;
-  return r;
-}
-
-__device__ __forceinline__ float seg_max(float v, unsigned m, int G) {
-  for (int off = 1; off < G; off <<= 1) v = fmaxf(v, __shfl_xor_sync(m, v, off, G));
-  return v;
-}
-__device__ __forceinline__ float seg_min(float v, unsigned m, int G) {
-  for (int off = 1; off < G; off <<= 1) v = fminf(v, __shfl_xor_sync(m, v, off, G));
-  return v;
-}
-__device__ __forceinline__ float seg_sum(float v, unsigned m, int G) {
-  for (int off = 1; off < G; off <<= 1) v = __fadd_rn(v, __shfl_xor_sync(m, v, off, G));
-  return v;
-}
-template <typename K>
-__device__ __forceinline__ K seg_kmax(K v, unsigned m, int G) {
-  for (int off = 1; off < G; off <<= 1) v = kmax(v, __shfl_xor_sync(m, v, off, G));
-  return v;
-}
-
-struct Params {
-  const void* gating;
-  const float* bias;
-  float* w_out;
-  int32_t* id_out;
-  long long T;
-  int E, G, GS, TG, K;
-  int renorm;
-  float scale;
-  int scoring;   // mcpuScoring
-  uint32_t idx_mask;  // (1 << idx_bits) - 1 for the 32-bit keys
-  float idx_quantum;  // 2^(idx_bits - 23): relative truncation of a 32-bit key
-};
-
-template <typename InT>
-__device__ __forceinline__ float load_one(const InT* p);
-template <>
-__device__ __forceinline__ float load_one<float>(const float* p) { return __ldg(p); }
-template <>
-__device__ __forceinline__ float load_one<__nv_bfloat16>(const __nv_bfloat16* p) {
-  return bf16_bits_to_float(__ldg(reinterpret_cast<const unsigned short*>(p)));
-}
+__device__ int g_router_error = 0;
 
 // Loads GS (<= GS_MAX) contiguous values into x[]; missing slots get 0.
 template <typename InT, int GS_MAX, bool kVec>
@@ -502,6 +310,84 @@ __global__ void __launch_bounds__(kThreads) grouped_topk_kernel(const Params p) 
   if (g == 0 && valid) write_outputs<kBf16, L>(p, token, ids, sc);
 }
 
+}  // namespace router
+}  // namespace mcpu
+
+#include "grouped_topk_tma.cuh"
+
+namespace mcpu {
+namespace router {
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+template <typename InT, int GS_MAX, bool kFast>
+static cudaError_t launch_tma_t(const Params& p, const CUtensorMap& tm, int tiles, int tpt, int smem,
+                                cudaStream_t st) {
+  auto kern = grouped_topk_tma_kernel<InT, GS_MAX, kFast>;
+  static int configured_smem = 0;  // per instantiation
+  if (configured_smem < smem) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    configured_smem = smem;
+  }
+  int dev = 0, sms = 148, per_sm = 1;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem);
+  if (per_sm < 1) per_sm = 1;
+  const int grid = tiles < sms * per_sm ? tiles : sms * per_sm;
+  kern<<<grid, kThreads, smem, st>>>(tm, p, tiles, tpt);
+  return cudaGetLastError();
+}
+
+template <typename InT, bool kFast>
+static cudaError_t launch_tma_gs(const Params& p, const CUtensorMap& tm, int tiles, int tpt, int smem,
+                                 cudaStream_t st) {
+  if (p.GS <= 8) return launch_tma_t<InT, 8, kFast>(p, tm, tiles, tpt, smem, st);
+  if (p.GS <= 16) return launch_tma_t<InT, 16, kFast>(p, tm, tiles, tpt, smem, st);
+  if (p.GS <= 32) return launch_tma_t<InT, 32, kFast>(p, tm, tiles, tpt, smem, st);
+  return launch_tma_t<InT, 64, kFast>(p, tm, tiles, tpt, smem, st);
+}
+
+// The TMA-fed kernel, when the layout allows it; *handled = false otherwise.
+static orError_t launch_tma(const Params& p, int dtype, bool fast, cudaStream_t st, bool* handled) {
+  *handled = false;
+  const int esz = dtype == MCPU_FLOAT32 ? 4 : 2;
+  if (reinterpret_cast<uintptr_t>(p.gating) % 16 != 0 || (p.E * esz) % 16 != 0 || p.E > 256)
+    return orSuccess;
+  if (p.bias && reinterpret_cast<uintptr_t>(p.bias) % 16 != 0) return orSuccess;
+  if (getenv("MCPU_ROUTER_NO_TMA")) return orSuccess;
+  static EncodeTiledFn enc =
+      reinterpret_cast<EncodeTiledFn>(driver_entry("cuTensorMapEncodeTiled"));
+  if (!enc) return orSuccess;
+  const int tpt = kThreads / p.G;
+  const TmaLayout L = tma_layout(tpt, p.E, esz);
+  if (L.total > 220 * 1024) return orSuccess;
+  CUtensorMap tm;
+  cuuint64_t gdim[2] = {static_cast<cuuint64_t>(p.E), static_cast<cuuint64_t>(p.T)};
+  cuuint64_t gstride[1] = {static_cast<cuuint64_t>(p.E) * esz};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(p.E), static_cast<cuuint32_t>(tpt)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(&tm, dtype == MCPU_FLOAT32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                   2, const_cast<void*>(p.gating), gdim, gstride, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return orSuccess;  // fall back to the direct-load kernel
+  const long long tiles = (p.T + tpt - 1) / tpt;
+  if (tiles > 0x7FFFFFFF / 2) return orSuccess;
+  cudaError_t e;
+  if (dtype == MCPU_FLOAT32)
+    e = fast ? launch_tma_gs<float, true>(p, tm, static_cast<int>(tiles), tpt, L.total, st)
+             : launch_tma_gs<float, false>(p, tm, static_cast<int>(tiles), tpt, L.total, st);
+  else
+    e = launch_tma_gs<__nv_bfloat16, false>(p, tm, static_cast<int>(tiles), tpt, L.total, st);
+  *handled = true;
+  return from_cuda(e, "grouped_topk launch");
+}
+
 template <typename InT, int GS_MAX, int L, bool kFast>
 static cudaError_t launch4(const Params& p, bool vec, cudaStream_t st) {
   const long long threads = p.T * p.G;
@@ -586,6 +472,9 @@ extern "C" orError_t mcpu_grouped_topk(const void* gating, int gating_dtype, int
                    (bias == nullptr || GS % 4 == 0);
   const bool fast = gating_dtype == MCPU_FLOAT32 && scoring_func == MCPU_SCORING_SIGMOID && bias;
   cudaStream_t st = as_cuda(stream);
+  bool handled = false;
+  orError_t te = router::launch_tma(p, gating_dtype, fast, st, &handled);
+  if (handled || te != orSuccess) return te;
   cudaError_t err;
   if (gating_dtype == MCPU_FLOAT32) {
     err = fast ? router::launch2<float, true>(p, vec, st) : router::launch2<float, false>(p, vec, st);
@@ -593,6 +482,15 @@ extern "C" orError_t mcpu_grouped_topk(const void* gating, int gating_dtype, int
     err = router::launch2<__nv_bfloat16, false>(p, vec, st);
   }
   return from_cuda(err, "grouped_topk launch");
+}
+
+orError_t router::read_error(int* flag, bool reset) {
+  MCPU_CUDA_TRY(cudaMemcpyFromSymbol(flag, router::g_router_error, sizeof(int)), "router error flag");
+  if (reset) {
+    const int zero = 0;
+    MCPU_CUDA_TRY(cudaMemcpyToSymbol(router::g_router_error, &zero, sizeof(int)), "router error flag reset");
+  }
+  return orSuccess;
 }
 
 extern "C" orError_t mcpu_grouped_topk_exact_rows(unsigned long long* count, int reset) {

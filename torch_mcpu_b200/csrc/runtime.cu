@@ -62,6 +62,15 @@ static orError_t poll_until(Query q, const char* what) {
   }
 }
 
+void* driver_entry(const char* name) {
+  void* ptr = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint(name, &ptr, cudaEnableDefault, &q) != cudaSuccess ||
+      q != cudaDriverEntryPointSuccess)
+    return nullptr;
+  return ptr;
+}
+
 }  // namespace mcpu
 
 using namespace mcpu;
@@ -69,6 +78,17 @@ using namespace mcpu;
 extern "C" {
 
 const char* mcpuGetLastErrorString(void) { return g_last_error; }
+
+orError_t mcpu_device_error(int* flag, int reset) {
+  MCPU_ARG_CHECK(flag != nullptr, "mcpu_device_error: flag is NULL");
+  int a = 0, b = 0;
+  orError_t e = gemm::read_error(&a, reset != 0);
+  if (e != orSuccess) return e;
+  e = router::read_error(&b, reset != 0);
+  if (e != orSuccess) return e;
+  *flag = a | b;
+  return orSuccess;
+}
 
 // ------------------------------------------------------------------ memory
 orError_t orMalloc(void** devPtr, size_t size) {

@@ -112,3 +112,76 @@ def rms_norm(out: torch.Tensor, x: torch.Tensor, weight: torch.Tensor, eps: floa
     T = x.numel() // H
     _lib.check(_lib.load().mcpu_rms_norm(out.data_ptr(), x.data_ptr(), weight.data_ptr(), T, H,
                                          float(eps), 1, _stream_handle(x.device)), "rms_norm")
+
+
+def _check_bf16_2d(t: torch.Tensor, name: str) -> None:
+    _require_device(t, name)
+    if t.dtype != torch.bfloat16 or t.dim() != 2:
+        raise RuntimeError(f"{name} must be a 2-D bfloat16 tensor")
+    if not t.is_contiguous():
+        raise RuntimeError(f"{name} must be contiguous")
+
+
+def mm_nt(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None,
+          bias: torch.Tensor | None = None) -> torch.Tensor:
+    """out = a @ b.T (+ bias), i.e. torch.mm(a, b.t()) for an nn.Linear weight
+    b [N, K]; aten::mm / aten::addmm of the reference (csrc/aten/ops/mm.cpp)."""
+    _check_bf16_2d(a, "a")
+    _check_bf16_2d(b, "b")
+    M, K = a.shape
+    N, K2 = b.shape
+    if K != K2:
+        raise RuntimeError(f"mm: a.size(1) ({K}) must match b.size(1) ({K2})")
+    if out is None:
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=a.device)
+    elif tuple(out.shape) != (M, N) or out.dtype != torch.bfloat16 or not out.is_contiguous():
+        raise RuntimeError(f"mm: out must be a contiguous bfloat16 [{M}, {N}] tensor")
+    lib = _lib.load()
+    s = _stream_handle(a.device)
+    if bias is None:
+        _lib.check(lib.mcpu_mm(a.data_ptr(), b.data_ptr(), out.data_ptr(), M, N, K, 1, s), "mm")
+    else:
+        if bias.numel() != N or bias.dtype != torch.bfloat16:
+            raise RuntimeError("addmm: bias must be bfloat16 [N]")
+        bias = bias.contiguous()
+        _lib.check(lib.mcpu_addmm(bias.data_ptr(), a.data_ptr(), b.data_ptr(), out.data_ptr(),
+                                  M, N, K, 1, s), "addmm")
+    return out
+
+
+def interleave_gate_up(w_gate_up: torch.Tensor, block: int = 128) -> torch.Tensor:
+    """[gate; up] stacked rows [2I, K] -> the 128-row interleaved layout the
+    fused gate/up GEMM reads (done once, when weights are loaded)."""
+    two_i, K = w_gate_up.shape
+    I = two_i // 2
+    if two_i != 2 * I or I % block != 0:
+        raise RuntimeError(f"interleave_gate_up: intermediate size {I} must be a multiple of {block}")
+    return (w_gate_up.view(2, I // block, block, K).transpose(0, 1).reshape(two_i, K).contiguous())
+
+
+def gemm_swiglu(x: torch.Tensor, w_gate_up_interleaved: torch.Tensor,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """out = silu(x @ Wg.T) * (x @ Wu.T) with the reference's bf16 roundings,
+    one kernel (see interleave_gate_up for the weight layout)."""
+    _check_bf16_2d(x, "x")
+    _check_bf16_2d(w_gate_up_interleaved, "w_gate_up")
+    M, K = x.shape
+    two_i, K2 = w_gate_up_interleaved.shape
+    if K != K2:
+        raise RuntimeError("gemm_swiglu: K mismatch")
+    I = two_i // 2
+    if out is None:
+        out = torch.empty(M, I, dtype=torch.bfloat16, device=x.device)
+    _lib.check(_lib.load().mcpu_gemm_swiglu(x.data_ptr(), w_gate_up_interleaved.data_ptr(),
+                                            out.data_ptr(), M, I, K, 1, _stream_handle(x.device)),
+               "gemm_swiglu")
+    return out
+
+
+def device_error(reset: bool = False) -> int:
+    """1 if a kernel gave up on a bounded wait since the last reset."""
+    import ctypes
+
+    f = ctypes.c_int(0)
+    _lib.check(_lib.load().mcpu_device_error(ctypes.byref(f), int(reset)), "device_error")
+    return int(f.value)
