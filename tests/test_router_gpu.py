@@ -209,3 +209,37 @@ def test_router_is_stream_ordered():
     s.synchronize()
     ow, oids, oties, _ = _oracle(cfg, gating, bias)
     _assert_parity(cfg, w.cpu().numpy(), ids.cpu().numpy(), ow, oids, oties, 1e-6)
+
+
+PATH_CASES = [
+    # (config, env) -- which kernel serves it is decided by the host dispatch
+    (C.RouterCfg("generic_tma_G2", 300, 64, 2, 1, 4, "sigmoid", True, True, 1.0), {}),
+    (C.RouterCfg("direct_E512", 200, 512, 8, 4, 8, "sigmoid", True, True, 2.5), {}),
+    (C.deepseek_v3(4096), {"MCPU_ROUTER_NO_TMA": "1"}),
+    (C.softmax160(777), {"MCPU_ROUTER_NO_TMA": "1"}),
+    (C.RouterCfg("all_groups_G4", 500, 128, 4, 4, 8, "sigmoid", True, True, 2.5), {}),
+    (C.RouterCfg("single_group_E64", 300, 64, 1, 1, 6, "softmax", False, True, 1.0), {}),
+]
+
+
+@pytest.mark.parametrize("cfg,env", PATH_CASES, ids=lambda v: v.name if hasattr(v, "name") else str(v))
+def test_router_every_kernel_path(cfg, env, monkeypatch):
+    for k, v in env.items():
+        monkeypatch.setenv(k, v)
+    gating, bias = C.router_inputs(cfg)
+    w, ids = _gpu(cfg, gating, bias)
+    ow, oids, oties, _ = _oracle(cfg, gating, bias)
+    _assert_parity(cfg, w, ids, ow, oids, oties, 1e-6)
+
+
+def test_router_repeated_calls_reuse_the_stream_worklist():
+    """The exact kernel resets the per-stream worklist after each call."""
+    m = _mcpu()
+    cfg = C.deepseek_v3(65536)
+    gating, bias = C.router_inputs(cfg)
+    g, b = gating.to(DEV), bias.to(DEV)
+    outs = [m.grouped_topk(g, g, 8, True, 8, 4, "sigmoid", 2.5, b) for _ in range(3)]
+    torch.cuda.synchronize()
+    for w, ids in outs[1:]:
+        assert torch.equal(ids, outs[0][1]) and torch.equal(w, outs[0][0])
+    assert m.device_error() == 0
