@@ -316,9 +316,6 @@ __global__ void __launch_bounds__(kThreads) grouped_topk_kernel(const Params p) 
 #include "grouped_topk_tma.cuh"
 #include "grouped_topk_g8.cuh"
 
-#include <map>
-#include <mutex>
-#include <utility>
 
 namespace mcpu {
 namespace router {
@@ -357,47 +354,7 @@ static cudaError_t launch_tma_gs(const Params& p, const CUtensorMap& tm, int til
   return launch_tma_t<InT, 64, kFast>(p, tm, tiles, tpt, smem, st);
 }
 
-// ---------------------------------------------------------------- hot + exact
-struct WsEntry {
-  int* hdr = nullptr;   // [0] count, [1] done ticket
-  int* rows = nullptr;
-  long long cap = 0;
-};
-
-// Worklist of the exact kernel, one per (device, stream): calls on one stream
-// are ordered, so they can share it; the exact kernel leaves it reset.
-static orError_t stream_workspace(cudaStream_t st, long long T, Worklist* wl) {
-  static std::mutex mu;
-  static std::map<std::pair<int, uintptr_t>, WsEntry> ws;
-  int dev = 0;
-  MCPU_CUDA_TRY(cudaGetDevice(&dev), "grouped_topk workspace");
-  std::lock_guard<std::mutex> lock(mu);
-  WsEntry& e = ws[{dev, reinterpret_cast<uintptr_t>(st)}];
-  if (e.cap < T) {
-    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-    cudaStreamIsCapturing(st, &cs);
-    MCPU_ARG_CHECK(cs == cudaStreamCaptureStatusNone,
-                   "grouped_topk: run one call with at least %lld tokens on this stream before "
-                   "capturing it in a CUDA graph (the stream's worklist must be allocated first)",
-                   T);
-    if (e.hdr) {
-      MCPU_CUDA_TRY(cudaStreamSynchronize(st), "grouped_topk workspace");
-      cudaFree(e.hdr);
-      cudaFree(e.rows);
-      e = WsEntry();
-    }
-    const long long cap = T < 4096 ? 4096 : T;
-    MCPU_CUDA_TRY(cudaMalloc(&e.hdr, 16), "grouped_topk workspace");
-    MCPU_CUDA_TRY(cudaMemset(e.hdr, 0, 16), "grouped_topk workspace");
-    MCPU_CUDA_TRY(cudaMalloc(&e.rows, cap * sizeof(int)), "grouped_topk workspace");
-    e.cap = cap;
-  }
-  wl->count = e.hdr;
-  wl->done = reinterpret_cast<unsigned*>(e.hdr + 1);
-  wl->rows = e.rows;
-  return orSuccess;
-}
-
+// ---------------------------------------------------------------- hot kernel
 static int device_sms() {
   int dev = 0, n = 148;
   cudaGetDevice(&dev);
@@ -405,25 +362,8 @@ static int device_sms() {
   return n > 0 ? n : 148;
 }
 
-template <typename InT>
-static cudaError_t launch_exact(const Params& p, const Worklist& wl, cudaStream_t st) {
-  const int smem = kExactWarps * (2 * p.E + p.G) * static_cast<int>(sizeof(float));
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(device_sms());
-  cfg.blockDim = dim3(kExactWarps * 32);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, grouped_topk_exact_kernel<InT>, p, wl);
-}
-
 template <typename InT, int G, int GS_MAX, bool kFast>
-static cudaError_t launch_hot_t(const Params& p, const CUtensorMap& tm, const Worklist& wl, int smem,
-                                cudaStream_t st) {
+static cudaError_t launch_hot_t(const Params& p, const CUtensorMap& tm, int smem, cudaStream_t st) {
   auto kern = grouped_topk_hot_kernel<InT, G, GS_MAX, kFast>;
   static int configured = 0;
   if (configured < smem) {
@@ -438,30 +378,28 @@ static cudaError_t launch_hot_t(const Params& p, const CUtensorMap& tm, const Wo
   if (per_sm < 1) per_sm = 1;
   const long long cap = static_cast<long long>(device_sms()) * per_sm;
   const int grid = static_cast<int>(tiles < cap ? tiles : cap);
-  kern<<<grid, kHotThreads, smem, st>>>(tm, p, static_cast<int>(tiles), wl);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
-  return launch_exact<InT>(p, wl, st);
+  kern<<<grid, kHotThreads, smem, st>>>(tm, p, static_cast<int>(tiles));
+  return cudaGetLastError();
 }
 
 // Which (segment width, group-size bound) the hot kernel is built for.
 template <typename InT, bool kFast>
-static bool dispatch_hot(const Params& p, const CUtensorMap& tm, const Worklist& wl, int smem,
-                         cudaStream_t st, cudaError_t* err) {
+static bool dispatch_hot(const Params& p, const CUtensorMap& tm, int smem, cudaStream_t st,
+                         cudaError_t* err) {
   const int G = p.G, GS = p.GS;
-  if (G == 8 && GS <= 8) { *err = launch_hot_t<InT, 8, 8, kFast>(p, tm, wl, smem, st); return true; }
-  if (G == 8 && GS <= 16) { *err = launch_hot_t<InT, 8, 16, kFast>(p, tm, wl, smem, st); return true; }
-  if (G == 8 && GS <= 32) { *err = launch_hot_t<InT, 8, 32, kFast>(p, tm, wl, smem, st); return true; }
+  if (G == 8 && GS <= 8) { *err = launch_hot_t<InT, 8, 8, kFast>(p, tm, smem, st); return true; }
+  if (G == 8 && GS <= 16) { *err = launch_hot_t<InT, 8, 16, kFast>(p, tm, smem, st); return true; }
+  if (G == 8 && GS <= 32) { *err = launch_hot_t<InT, 8, 32, kFast>(p, tm, smem, st); return true; }
   if constexpr (sizeof(InT) == 4) {
-    if (G == 16 && GS <= 16) { *err = launch_hot_t<InT, 16, 16, kFast>(p, tm, wl, smem, st); return true; }
-    if (G == 32 && GS <= 8) { *err = launch_hot_t<InT, 32, 8, kFast>(p, tm, wl, smem, st); return true; }
-    if (G == 4 && GS <= 32) { *err = launch_hot_t<InT, 4, 32, kFast>(p, tm, wl, smem, st); return true; }
+    if (G == 16 && GS <= 16) { *err = launch_hot_t<InT, 16, 16, kFast>(p, tm, smem, st); return true; }
+    if (G == 32 && GS <= 8) { *err = launch_hot_t<InT, 32, 8, kFast>(p, tm, smem, st); return true; }
+    if (G == 4 && GS <= 32) { *err = launch_hot_t<InT, 4, 32, kFast>(p, tm, smem, st); return true; }
   }
   return false;
 }
 
-// The specialised hot kernel plus the exact worklist kernel, when the
-// configuration allows it; *handled = false otherwise.
+// The specialised hot kernel, when the configuration allows it;
+// *handled = false otherwise.
 static orError_t launch_hot(Params p, int dtype, bool fast, cudaStream_t st, bool* handled) {
   *handled = false;
   const int esz = dtype == MCPU_FLOAT32 ? 4 : 2;
@@ -493,16 +431,13 @@ static orError_t launch_hot(Params p, int dtype, bool fast, cudaStream_t st, boo
           CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return orSuccess;
-  Worklist wl;
-  orError_t we = stream_workspace(st, p.T, &wl);
-  if (we != orSuccess) return we;
   cudaError_t err = cudaSuccess;
   bool ok;
   if (dtype == MCPU_FLOAT32)
-    ok = fast ? dispatch_hot<float, true>(p, tm, wl, L.total, st, &err)
-              : dispatch_hot<float, false>(p, tm, wl, L.total, st, &err);
+    ok = fast ? dispatch_hot<float, true>(p, tm, L.total, st, &err)
+              : dispatch_hot<float, false>(p, tm, L.total, st, &err);
   else
-    ok = dispatch_hot<__nv_bfloat16, false>(p, tm, wl, L.total, st, &err);
+    ok = dispatch_hot<__nv_bfloat16, false>(p, tm, L.total, st, &err);
   if (!ok) return orSuccess;
   *handled = true;
   return from_cuda(err, "grouped_topk launch");

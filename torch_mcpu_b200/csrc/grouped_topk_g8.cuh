@@ -1,21 +1,24 @@
-// grouped_topk: specialised TMA-fed kernel + exact worklist kernel
-// (included by grouped_topk.cu).
+// grouped_topk: the specialised TMA-fed kernel (included by grouped_topk.cu).
 //
-// Hot kernel.  A G-lane segment serves one token (G a compile-time power of
-// two); a 128-thread CTA holds 128/G tokens per tile and loops over tiles
+// A G-lane segment serves one token (G a compile-time power of two); a
+// 128-thread CTA holds 128/G tokens per tile and loops over tiles
 // persistently while one thread keeps a 2-stage TMA ring of [128/G, E] tiles
-// filled.  Lane g of a segment owns group g.  The expert pick works on the
-// candidate list (keys >= L0 - delta, see grouped_topk_tma.cuh) ranked by
-// direct comparison.  A token whose fast result cannot be certified, or whose
-// candidate list overflows, is appended to a worklist and left to the exact
-// kernel; the hot kernel itself carries no exact-arithmetic code.
+// filled.  Lane g of a segment owns group g and keeps its experts' keys in
+// registers.
 //
-// Exact kernel.  One warp per worklist row: exact keys (correctly rounded
-// sigmoid, or the exact softmax definition), group pick and k rounds of warp
-// argmax, all through per-warp shared memory.  It is launched right behind the
-// hot kernel with programmatic dependent launch and waits on the hot kernel's
-// completion (griddepcontrol.wait) before reading the worklist; the last CTA
-// to finish resets the worklist counter for the next call on the stream.
+// Expert pick: every selected group contributes its two best experts, so with
+// 2 * topk_group >= topk the k-th best candidate is at least L0 = min over
+// selected groups of the group's second-best key; only keys >= L0 - delta can
+// be among the top k.  Each lane marks those slots in a 32-bit mask, writes
+// them (as 64-bit packed value/index keys) to the token's list in shared
+// memory, and every candidate is ranked by direct comparison.
+//
+// Exactness (fp32 sigmoid + bias): the fast keys are within eps(|key|) =
+// 2^-21 + 2^-22 |key| of the exact ones.  When both selection margins exceed
+// 4 eps the fast pick is provably the exact pick.  Otherwise the row is
+// refined in place: exact keys are computed only for the experts that can
+// still matter (within 4 eps of a group's second best, to get exact group
+// scores, and the candidate list), and the pick is redone on exact keys.
 #pragma once
 
 #include "sm100.cuh"
@@ -25,16 +28,10 @@ namespace router {
 
 constexpr int kHotThreads = 128;
 constexpr int kHotStages = 2;
-constexpr int kCandStride = kCap + 1;  // padded: segments of a warp hit distinct banks
-
-struct Worklist {
-  int* count;         // rows appended by the hot kernel
-  unsigned* done;     // CTA ticket of the exact kernel
-  int* rows;          // capacity >= num_tokens
-};
+constexpr int kCandStride = kCap + 1;  // padded: the segments of a warp hit distinct banks
 
 struct HotLayout {
-  int tile_bytes, bias_off, ck_off, ci_off, selk_off, seli_off, wbuf_off, ninth_off, bar_off, total;
+  int tile_bytes, bias_off, cand_off, sel_off, wbuf_off, bar_off, total;
 };
 
 __host__ __device__ inline HotLayout hot_layout(int tpt, int E, int esz) {
@@ -43,52 +40,51 @@ __host__ __device__ inline HotLayout hot_layout(int tpt, int E, int esz) {
   int off = kHotStages * L.tile_bytes;
   L.bias_off = off;
   off += (E * 4 + 15) & ~15;
-  L.ck_off = off;
-  off += tpt * kCandStride * 4;
-  L.ci_off = off;
-  off += ((tpt * kCandStride * 2) + 15) & ~15;
-  L.selk_off = off;
-  off += tpt * (kMaxK + 1) * 4;
-  L.seli_off = off;
-  off += tpt * (kMaxK + 1) * 4;
+  L.cand_off = off;
+  off += tpt * kCandStride * 8;
+  L.sel_off = off;
+  off += tpt * (kMaxK + 1) * 8;
   L.wbuf_off = off;
-  off += tpt * (kMaxK + 1) * 4;
-  L.ninth_off = off;
-  off += ((tpt * 4) + 15) & ~15;
+  off += ((tpt * (kMaxK + 1) * 4) + 15) & ~15;
   L.bar_off = off;
   off += kHotStages * 8 + 16;
   L.total = off + 1024;
   return L;
 }
 
-__device__ __forceinline__ void pdl_launch_dependents() {
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+__device__ __forceinline__ unsigned long long pack_key(float f, int idx) {
+  return (static_cast<unsigned long long>(orderable(f)) << 32) |
+         static_cast<unsigned long long>(0xFFFFFFFFu - static_cast<uint32_t>(idx));
+}
+__device__ __forceinline__ int packed_index(unsigned long long k) {
+  return static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(k));
+}
+__device__ __forceinline__ float packed_value(unsigned long long k) {
+  const uint32_t u = static_cast<uint32_t>(k >> 32);
+  return __uint_as_float((u & 0x80000000u) ? (u & 0x7FFFFFFFu) : ~u);
 }
 
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Error bound of a fast key against the exact one: |fast - exact| <= eps(|key|).
+__device__ __forceinline__ float key_eps(float mag) { return 0x1p-21f + 0x1p-22f * mag; }
 
 template <typename InT, int G, int GS_MAX, bool kFast>
-__global__ void __launch_bounds__(kHotThreads, 4) grouped_topk_hot_kernel(
-    const __grid_constant__ CUtensorMap tm, const Params p, const int tiles, const Worklist wl) {
+__global__ void __launch_bounds__(kHotThreads, 6) grouped_topk_hot_kernel(
+    const __grid_constant__ CUtensorMap tm, const Params p, const int tiles) {
   constexpr bool kBf16 = sizeof(InT) == 2;
   constexpr int VE = 16 / sizeof(InT);
   constexpr int NCH_MAX = (GS_MAX + VE - 1) / VE;
   constexpr int TPT = kHotThreads / G;
   constexpr unsigned kSegBits = (G == 32) ? 0xFFFFFFFFu : ((1u << G) - 1u);
-
-  pdl_launch_dependents();  // the exact kernel may be scheduled now; it waits for us
+  static_assert(GS_MAX <= 32, "slot masks are 32 bits");
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t ra = sm100::smem_u32(smem_raw);
   uint8_t* base = smem_raw + ((1024 - (ra & 1023)) & 1023);
   const HotLayout L = hot_layout(TPT, p.E, sizeof(InT));
   float* sbias = reinterpret_cast<float*>(base + L.bias_off);
-  float* ck = reinterpret_cast<float*>(base + L.ck_off);
-  uint16_t* ci = reinterpret_cast<uint16_t*>(base + L.ci_off);
-  float* selk = reinterpret_cast<float*>(base + L.selk_off);
-  int* seli = reinterpret_cast<int*>(base + L.seli_off);
+  unsigned long long* cand = reinterpret_cast<unsigned long long*>(base + L.cand_off);
+  unsigned long long* sel = reinterpret_cast<unsigned long long*>(base + L.sel_off);
   float* wbuf = reinterpret_cast<float*>(base + L.wbuf_off);
-  float* ninth = reinterpret_cast<float*>(base + L.ninth_off);
   uint64_t* full = reinterpret_cast<uint64_t*>(base + L.bar_off);
   int* abort_flag = reinterpret_cast<int*>(base + L.bar_off + kHotStages * 8);
 
@@ -102,6 +98,7 @@ __global__ void __launch_bounds__(kHotThreads, 4) grouped_topk_hot_kernel(
   const int nch = GS / VE;
   const int gshift = g % (nch > 0 ? nch : 1);
   const bool vec_layout = (GS % VE) == 0;
+  const bool two_best = GS >= 2 && 2 * TG >= K;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kHotStages; ++s) sm100::mbar_init(&full[s], 1);
@@ -149,8 +146,27 @@ __global__ void __launch_bounds__(kHotThreads, 4) grouped_topk_hot_kernel(
       for (int off = 1; off < G; off <<= 1) sum = __fadd_rn(sum, __shfl_xor_sync(segmask, sum, off, G));
       row_sum = sum;
     }
+    auto live = [&](int s) -> bool { return vec_layout ? (s / VE) < nch : s < GS; };
+    auto local_of = [&](int s) -> int {
+      if (!vec_layout) return s;
+      const int c = s / VE;
+      int cc = c + gshift;
+      if (cc >= nch) cc -= nch;
+      return cc * VE + (s - c * VE);
+    };
+    // key of local expert j of this lane's group: the ranking key of the
+    // kernel's mode, or (exact = true) the exact key
+    auto key_of = [&](int j, bool exact) -> float {
+      const float xv = smem_elem<InT>(grp, j);
+      if (kFast && !exact) return fast_key(xv, bgrp[j]);
+      if (!has_bias) return xv;
+      float sc = p.scoring == MCPU_SCORING_SIGMOID ? sigmoid_exact_call(xv)
+                                                   : __fdiv_rn(expf(xv - row_max), row_sum);
+      if (kBf16) sc = round_bf16(sc);
+      return __fadd_rn(sc, bgrp[j]);
+    };
 
-    // ---- keys + the group's two best, chunk by chunk from shared memory
+    // ---- keys (fast, or exact in the exact-key modes) + the group's two best
     float key[GS_MAX];
     float m1 = -INFINITY, m2 = -INFINITY;
     if (vec_layout) {
@@ -209,138 +225,170 @@ __global__ void __launch_bounds__(kHotThreads, 4) grouped_topk_hot_kernel(
     } else {
 #pragma unroll
       for (int s = 0; s < GS_MAX; ++s) {
-        float k = -INFINITY;
-        if (s < GS) {
-          const float xv = smem_elem<InT>(grp, s), bv = bgrp[s];
-          if constexpr (kFast) {
-            k = fast_key(xv, bv);
-          } else if (has_bias) {
-            float sc = p.scoring == MCPU_SCORING_SIGMOID ? sigmoid_exact_call(xv)
-                                                         : __fdiv_rn(expf(xv - row_max), row_sum);
-            if (kBf16) sc = round_bf16(sc);
-            k = __fadd_rn(sc, bv);
-          } else {
-            k = xv;
-          }
-        }
+        const float k = s < GS ? key_of(s, !kFast) : -INFINITY;
         key[s] = k;
         m2 = fmaxf(m2, fminf(m1, k));
         m1 = fmaxf(m1, k);
       }
     }
-    auto local_of = [&](int s) -> int {
-      if (!vec_layout) return s;
-      const int c = s / VE;
-      int cc = c + gshift;
-      if (cc >= nch) cc -= nch;
-      return cc * VE + (s - c * VE);
-    };
 
-    // ---- group pick (ties to the lower group index)
-    const float gs = has_bias ? __fadd_rn(m1, m2) : m1;
-    int rank = 0;
+    unsigned long long* tc = cand + tok * kCandStride;
+    unsigned long long* ts = sel + tok * (kMaxK + 1);
+    bool exact = !kFast;  // are the group scores and candidate keys exact?
+    bool slow = false;
+#pragma unroll 1
+    for (;;) {
+      float gsv, m2v;
+      if (kFast && exact) {
+        // exact two best of this group: only experts whose fast key is within
+        // 4 eps of the fast second best can be among the exact two best
+        const float lim = m2 - 4.0f * key_eps(fabsf(m2));
+        uint32_t near = 0;
 #pragma unroll
-    for (int j = 0; j < G; ++j) {
-      const float o = __shfl_sync(segmask, gs, j, G);
-      rank += (o > gs) || (o == gs && j < g);
-    }
-    const bool gsel = rank < TG;
-    bool ok = true;
-    if constexpr (kFast) {
-      float lo = gsel ? gs : INFINITY, hi = gsel ? -INFINITY : gs;
+        for (int s = 0; s < GS_MAX; ++s) near |= (key[s] >= lim) ? (1u << s) : 0u;
+        float e1 = -INFINITY, e2 = -INFINITY;
+#pragma unroll 1
+        for (uint32_t m = near; m; m &= m - 1) {
+          const float ke = key_of(local_of(__ffs(m) - 1), true);
+          e2 = fmaxf(e2, fminf(e1, ke));
+          e1 = fmaxf(e1, ke);
+        }
+        gsv = __fadd_rn(e1, e2);
+        m2v = e2;
+      } else {
+        gsv = has_bias ? __fadd_rn(m1, m2) : m1;
+        m2v = m2;
+      }
+      // group pick (ties to the lower group index)
+      int rank = 0;
+#pragma unroll
+      for (int j = 0; j < G; ++j) {
+        const float o = __shfl_sync(segmask, gsv, j, G);
+        rank += (o > gsv) || (o == gsv && j < g);
+      }
+      const bool gsel = rank < TG;
+      bool ok = true;
+      if (!exact) {
+        float lo = gsel ? gsv : INFINITY, hi = gsel ? -INFINITY : gsv;
+#pragma unroll
+        for (int off = 1; off < G; off <<= 1) {
+          lo = fminf(lo, __shfl_xor_sync(segmask, lo, off, G));
+          hi = fmaxf(hi, __shfl_xor_sync(segmask, hi, off, G));
+        }
+        if (hi != -INFINITY) ok = (lo - hi) > 4.0f * key_eps(fmaxf(fabsf(lo), fabsf(hi)));
+      }
+      // candidates: keys >= L0 - delta in the selected groups, where
+      // L0 = min over selected groups of the second best key
+      float l0 = gsel ? m2v : INFINITY;
+#pragma unroll
+      for (int off = 1; off < G; off <<= 1) l0 = fminf(l0, __shfl_xor_sync(segmask, l0, off, G));
+      if (!two_best) l0 = -INFINITY;
+      const float thr = kFast ? l0 - 4.0f * key_eps(fabsf(l0)) : l0;
+      uint32_t mask = 0;
+#pragma unroll
+      for (int s = 0; s < GS_MAX; ++s) mask |= (key[s] >= thr) ? (1u << s) : 0u;
+      if (!gsel) mask = 0;
+      const int c = __popc(mask);
+      int incl = c;
 #pragma unroll
       for (int off = 1; off < G; off <<= 1) {
-        lo = fminf(lo, __shfl_xor_sync(segmask, lo, off, G));
-        hi = fmaxf(hi, __shfl_xor_sync(segmask, hi, off, G));
+        const int o = __shfl_up_sync(segmask, incl, off, G);
+        if (g >= off) incl += o;
       }
-      if (hi != -INFINITY) ok = (lo - hi) > (0x1p-18f + 0x1p-19f * fmaxf(fabsf(lo), fabsf(hi)));
-    }
-
-    // ---- candidates: keys >= L0 - delta in the selected groups
-    float l0 = gsel ? m2 : INFINITY;
+      const int C = __shfl_sync(segmask, incl, G - 1, G);
+      if (C > kCap) {
+        if (!exact) {  // many near-equal keys: settle it on exact keys
+          exact = true;
+          slow = true;
+          continue;
+        }
+        // degenerate input (more than kCap exact near-ties): k rounds of
+        // segment argmax over exact keys, evaluated slot by slot
+        uint32_t livemask = 0;
 #pragma unroll
-    for (int off = 1; off < G; off <<= 1) l0 = fminf(l0, __shfl_xor_sync(segmask, l0, off, G));
-    if (!(GS >= 2 && 2 * TG >= K)) l0 = -INFINITY;
-    const float thr = kFast ? l0 - (0x1p-19f + 0x1p-20f * fabsf(l0)) : l0;
-    int c = 0;
+        for (int s = 0; s < GS_MAX; ++s) livemask |= live(s) ? (1u << s) : 0u;
+        if (!gsel) livemask = 0;
+        unsigned long long last = ~0ull;
+#pragma unroll 1
+        for (int r = 0; r < K; ++r) {
+          unsigned long long best = 0;
+#pragma unroll 1
+          for (uint32_t m = livemask; m; m &= m - 1) {
+            const int j = local_of(__ffs(m) - 1);
+            const unsigned long long pk = pack_key(kFast ? key_of(j, true) : key_of(j, !kFast), g * GS + j);
+            if (pk < last && pk > best) best = pk;
+          }
 #pragma unroll
-    for (int s = 0; s < GS_MAX; ++s) c += (gsel && key[s] >= thr) ? 1 : 0;
-    int incl = c;
-#pragma unroll
-    for (int off = 1; off < G; off <<= 1) {
-      const int o = __shfl_up_sync(segmask, incl, off, G);
-      if (g >= off) incl += o;
-    }
-    const int C = __shfl_sync(segmask, incl, G - 1, G);
-    float* tck = ck + tok * kCandStride;
-    uint16_t* tci = ci + tok * kCandStride;
-    float* tsk = selk + tok * (kMaxK + 1);
-    int* tsi = seli + tok * (kMaxK + 1);
-    const bool fits = C <= kCap;
-    if (fits) {
+          for (int off = 1; off < G; off <<= 1) {
+            const unsigned long long o = __shfl_xor_sync(segmask, best, off, G);
+            best = o > best ? o : best;
+          }
+          if (g == 0) ts[r] = best;
+          last = best;
+        }
+        __syncwarp(segmask);
+        break;
+      }
+      // write this lane's candidates at its prefix position
       int pos = incl - c;
-#pragma unroll
-      for (int s = 0; s < GS_MAX; ++s) {
-        if (gsel && key[s] >= thr) {
-          tck[pos] = key[s];
-          tci[pos] = static_cast<uint16_t>(g * GS + local_of(s));
-          ++pos;
-        }
+      for (uint32_t m = mask; m; m &= m - 1) {
+        const int j = local_of(__ffs(m) - 1);
+        tc[pos++] = pack_key(key_of(j, exact), g * GS + j);
       }
       __syncwarp(segmask);
+      // rank every candidate against all others (packed keys: one compare)
       for (int q = g; q < C; q += G) {
-        const float v = tck[q];
-        const int iv = tci[q];
+        const unsigned long long v = tc[q];
         int r = 0;
-        for (int k2 = 0; k2 < C; ++k2) r += ranks_before(tck[k2], tci[k2], v, iv) ? 1 : 0;
-        if (r < K) {
-          tsk[r] = v;
-          tsi[r] = iv;
-        } else if (r == K) {
-          ninth[tok] = v;
-        }
+        for (int k2 = 0; k2 < C; ++k2) r += tc[k2] > v ? 1 : 0;
+        if (r <= K) ts[r] = v;
       }
       __syncwarp(segmask);
-      if (kFast && C > K) {
-        const float k8 = tsk[K - 1], k9 = ninth[tok];
-        ok = ok && (k8 - k9) > (0x1p-19f + 0x1p-20f * fmaxf(fabsf(k8), fabsf(k9)));
+      if (!exact) {
+        if (C > K) {
+          const float k8 = packed_value(ts[K - 1]), k9 = packed_value(ts[K]);
+          ok = ok && (k8 - k9) > 4.0f * key_eps(fmaxf(fabsf(k8), fabsf(k9)));
+        }
+        if (!ok) {
+          exact = true;
+          slow = true;
+          continue;
+        }
       }
+      break;
     }
-    const bool certified = fits && ok;
+    if (slow && g == 0 && valid) atomicAdd(&g_exact_rows, 1ull);
 
-    if (!certified) {
-      if (g == 0 && valid) wl.rows[atomicAdd(wl.count, 1)] = static_cast<int>(token);
-    } else {
-      float* tw = wbuf + tok * (kMaxK + 1);
+    // ---- weights, renormalisation, scaling, stores
+    float* tw = wbuf + tok * (kMaxK + 1);
+    for (int k = g; k < K; k += G) {
+      const float xv = smem_elem<InT>(row, packed_index(ts[k]));
+      float sc;
+      if (p.scoring == MCPU_SCORING_SIGMOID)
+        sc = (kFast && !slow) ? sigmoid_accurate(xv) : sigmoid_exact_call(xv);
+      else
+        sc = __fdiv_rn(expf(xv - row_max), row_sum);
+      tw[k] = kBf16 ? round_bf16(sc) : sc;
+    }
+    __syncwarp(segmask);
+    float sum = 0.0f;
+    if (p.renorm) {
+      for (int k = 0; k < K; ++k) sum = __fadd_rn(sum, tw[k]);
+      if (kBf16) sum = round_bf16(sum);
+    }
+    if (valid) {
       for (int k = g; k < K; k += G) {
-        const float xv = smem_elem<InT>(row, tsi[k]);
-        float sc;
-        if (p.scoring == MCPU_SCORING_SIGMOID)
-          sc = kFast ? sigmoid_accurate(xv) : sigmoid_exact_call(xv);
-        else
-          sc = __fdiv_rn(expf(xv - row_max), row_sum);
-        tw[k] = kBf16 ? round_bf16(sc) : sc;
-      }
-      __syncwarp(segmask);
-      float sum = 0.0f;
-      if (p.renorm) {
-        for (int k = 0; k < K; ++k) sum = __fadd_rn(sum, tw[k]);
-        if (kBf16) sum = round_bf16(sum);
-      }
-      if (valid) {
-        for (int k = g; k < K; k += G) {
-          float w = tw[k];
-          if (p.renorm) {
-            w = __fdiv_rn(w, sum);
-            if (kBf16) w = round_bf16(w);
-          }
-          if (p.scale != 1.0f) {
-            w = __fmul_rn(w, p.scale);
-            if (kBf16) w = round_bf16(w);
-          }
-          p.w_out[token * K + k] = w;
-          p.id_out[token * K + k] = tsi[k];
+        float w = tw[k];
+        if (p.renorm) {
+          w = __fdiv_rn(w, sum);
+          if (kBf16) w = round_bf16(w);
         }
+        if (p.scale != 1.0f) {
+          w = __fmul_rn(w, p.scale);
+          if (kBf16) w = round_bf16(w);
+        }
+        p.w_out[token * K + k] = w;
+        p.id_out[token * K + k] = packed_index(ts[k]);
       }
     }
     __syncthreads();
@@ -354,143 +402,6 @@ __global__ void __launch_bounds__(kHotThreads, 4) grouped_topk_hot_kernel(
       for (uint32_t n = 0; n < sm100::kSpinLimit && !sm100::mbar_try_wait(&full[j & 1], (j >> 1) & 1);
            ++n) {
       }
-    }
-  }
-}
-
-// ------------------------------------------------------------------ exact kernel
-constexpr int kExactWarps = 4;
-
-template <typename InT>
-__global__ void __launch_bounds__(kExactWarps * 32) grouped_topk_exact_kernel(const Params p,
-                                                                             const Worklist wl) {
-  extern __shared__ float xsm[];  // per warp: key[E], score[E], gsc[G]
-  pdl_wait();                      // the hot kernel's worklist is complete and visible
-  constexpr bool kBf16 = sizeof(InT) == 2;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int E = p.E, G = p.G, GS = p.GS, K = p.K;
-  float* skey = xsm + warp * (2 * E + G);
-  float* ssc = skey + E;
-  float* sgs = ssc + E;
-  const int n = *reinterpret_cast<volatile int*>(wl.count);
-  const int nwarps = gridDim.x * kExactWarps;
-  const bool has_bias = p.bias != nullptr;
-  for (int item = blockIdx.x * kExactWarps + warp; item < n; item += nwarps) {
-    const long long token = wl.rows[item];
-    const InT* row = reinterpret_cast<const InT*>(p.gating) + token * E;
-    float row_max = 0.0f, row_sum = 1.0f;
-    if (p.scoring == MCPU_SCORING_SOFTMAX) {
-      float m = -INFINITY;
-      for (int e = lane; e < E; e += 32) m = fmaxf(m, load_one<InT>(row + e));
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, off));
-      row_max = m;
-      // fixed summation order: lane-strided partial sums, then a fixed tree
-      float s = 0.0f;
-      for (int e = lane; e < E; e += 32) s = __fadd_rn(s, expf(load_one<InT>(row + e) - row_max));
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xFFFFFFFFu, s, off));
-      row_sum = s;
-    }
-    for (int e = lane; e < E; e += 32) {
-      const float xv = load_one<InT>(row + e);
-      float sc = p.scoring == MCPU_SCORING_SIGMOID ? sigmoid_exact_call(xv)
-                                                   : __fdiv_rn(expf(xv - row_max), row_sum);
-      if (kBf16) sc = round_bf16(sc);
-      ssc[e] = sc;
-      skey[e] = has_bias ? __fadd_rn(sc, __ldg(p.bias + e)) : xv;
-    }
-    __syncwarp();
-    for (int gi = lane; gi < G; gi += 32) {
-      float m1 = -INFINITY, m2 = -INFINITY;
-      for (int j = 0; j < GS; ++j) {
-        const float v = skey[gi * GS + j];
-        m2 = fmaxf(m2, fminf(m1, v));
-        m1 = fmaxf(m1, v);
-      }
-      sgs[gi] = has_bias ? __fadd_rn(m1, m2) : m1;
-    }
-    __syncwarp();
-    // group pick: rank of each group among all G (ties to the lower index)
-    unsigned long long sel_lo = 0;  // bit g: group g selected (G <= 64 supported here)
-    for (int gi = lane; gi < G; gi += 32) {
-      const float v = sgs[gi];
-      int r = 0;
-      for (int j = 0; j < G; ++j) r += ranks_before(sgs[j], j, v, gi) ? 1 : 0;
-      if (r < p.TG) sel_lo |= 1ull << gi;
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) sel_lo |= __shfl_xor_sync(0xFFFFFFFFu, sel_lo, off);
-    // k rounds of warp argmax over the experts of the selected groups
-    float lk = INFINITY;
-    int li = -1;
-    int ids[kMaxK];
-#pragma unroll
-    for (int r = 0; r < kMaxK; ++r) ids[r] = 0;
-    for (int r = 0; r < K; ++r) {
-      float bk = -INFINITY;
-      int bi = 0x7FFFFFFF;
-      for (int e = lane; e < E; e += 32) {
-        if (!((sel_lo >> (e / GS)) & 1ull)) continue;
-        const float v = skey[e];
-        const bool after = v < lk || (v == lk && e > li);
-        if (after && ranks_before(v, e, bk, bi)) {
-          bk = v;
-          bi = e;
-        }
-      }
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) {
-        const float ok2 = __shfl_xor_sync(0xFFFFFFFFu, bk, off);
-        const int oi2 = __shfl_xor_sync(0xFFFFFFFFu, bi, off);
-        if (ranks_before(ok2, oi2, bk, bi)) {
-          bk = ok2;
-          bi = oi2;
-        }
-      }
-#pragma unroll
-      for (int q = 0; q < kMaxK; ++q)
-        if (q == r) ids[q] = bi;
-      lk = bk;
-      li = bi;
-    }
-    if (lane == 0) {
-      float w[kMaxK];
-      float sum = 0.0f;
-#pragma unroll
-      for (int k = 0; k < kMaxK; ++k) {
-        w[k] = k < K ? ssc[ids[k]] : 0.0f;
-        if (k < K) sum = __fadd_rn(sum, w[k]);
-      }
-      if (kBf16) sum = round_bf16(sum);
-#pragma unroll
-      for (int k = 0; k < kMaxK; ++k) {
-        if (k >= K) continue;
-        float v = w[k];
-        if (p.renorm) {
-          v = __fdiv_rn(v, sum);
-          if (kBf16) v = round_bf16(v);
-        }
-        if (p.scale != 1.0f) {
-          v = __fmul_rn(v, p.scale);
-          if (kBf16) v = round_bf16(v);
-        }
-        p.w_out[token * K + k] = v;
-        p.id_out[token * K + k] = ids[k];
-      }
-      atomicAdd(&g_exact_rows, 1ull);
-    }
-    __syncwarp();
-  }
-  // the last CTA to finish resets the worklist for the next call
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    const unsigned ticket = atomicAdd(wl.done, 1u);
-    if (ticket == gridDim.x - 1) {
-      *wl.count = 0;
-      *wl.done = 0u;
-      __threadfence();
     }
   }
 }
