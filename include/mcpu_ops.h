@@ -25,7 +25,15 @@ extern "C" {
 
 typedef enum mcpuDtype {
   MCPU_FLOAT32 = 0,
-  MCPU_BFLOAT16 = 1
+  MCPU_BFLOAT16 = 1,
+  MCPU_FLOAT16 = 2,
+  MCPU_INT32 = 3,
+  MCPU_INT64 = 4,
+  MCPU_UINT8 = 5,
+  MCPU_BOOL = 6,
+  MCPU_FLOAT64 = 7,
+  MCPU_INT8 = 8,
+  MCPU_INT16 = 9
 } mcpuDtype;
 
 typedef enum mcpuScoring {
@@ -142,6 +150,40 @@ OPENREG_EXPORT orError_t mcpu_gemm_swiglu(const void* x, const void* w_gate_up, 
  * its output incomplete.  No counterpart in the reference, whose host
  * worker threads report hangs through orStreamSynchronize's timeout. */
 OPENREG_EXPORT orError_t mcpu_device_error(int* flag, int reset);
+
+/*
+ * Tensor plumbing of the mcpu device (all asynchronous on `stream`).
+ *
+ * mcpu_copy_strided: dst[i] = convert(src[i]) over an ndim <= 8 index space
+ * with element strides (either side may be non-contiguous); dtype
+ * conversion follows torch's rules (through fp32 for bf16/fp16, truncation
+ * toward zero for float -> int, nonzero -> 1 for bool).  Replaces the
+ * device-side cases of _copy_from (csrc/aten/native/Minimal.cpp:393-484).
+ *
+ * mcpu_fill: every element of a strided view set to one value.  Replaces
+ * fill_ / zero_ (csrc/aten/ops/fill.cpp:12-44, unary_out.cpp:239-267).
+ */
+OPENREG_EXPORT orError_t mcpu_copy_strided(const void* src, int src_dtype, void* dst, int dst_dtype,
+                                           int ndim, const int64_t* sizes,
+                                           const int64_t* src_strides, const int64_t* dst_strides,
+                                           orStream_t stream);
+OPENREG_EXPORT orError_t mcpu_fill(void* dst, int dtype, int ndim, const int64_t* sizes,
+                                   const int64_t* strides, double fvalue, int64_t ivalue,
+                                   int value_is_float, orStream_t stream);
+
+/*
+ * Elementwise ops on contiguous buffers of n elements (fp32 or bf16):
+ * sigmoid = 1 / (1 + exp(-x)), silu = x / (1 + exp(-x)) in fp32 with exp
+ * correctly rounded (the raw loops of csrc/aten/ops/unary_out.cpp:46-51,
+ * sigmoid_out 415-430, silu_out 456-470; bf16 results are rounded from the
+ * fp32 value), mul = a * b rounded to the dtype (binary_out.cpp:544-560).
+ */
+OPENREG_EXPORT orError_t mcpu_sigmoid(void* out, const void* x, int64_t n, int dtype,
+                                      orStream_t stream);
+OPENREG_EXPORT orError_t mcpu_silu(void* out, const void* x, int64_t n, int dtype,
+                                   orStream_t stream);
+OPENREG_EXPORT orError_t mcpu_mul(void* out, const void* a, const void* b, int64_t n, int dtype,
+                                  orStream_t stream);
 
 #ifdef __cplusplus
 }  // extern "C"

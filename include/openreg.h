@@ -99,6 +99,15 @@ OPENREG_EXPORT orError_t orPointerGetAttributes(
 OPENREG_EXPORT orError_t orMemoryUnprotect(void* devPtr);
 OPENREG_EXPORT orError_t orMemoryProtect(void* devPtr);
 
+/* Stream-ordered allocation (not in the reference's C-ABI; it backs the
+ * caching allocator of csrc/runtime/DeviceCachingAllocator.cpp):
+ * cudaMallocAsync / cudaFreeAsync on the device's default memory pool, whose
+ * release threshold is raised so freed memory stays cached; orMemPoolTrim
+ * returns cached memory above keep_bytes to the driver (empty_cache). */
+OPENREG_EXPORT orError_t orMallocAsync(void** devPtr, size_t size, orStream_t stream);
+OPENREG_EXPORT orError_t orFreeAsync(void* devPtr, orStream_t stream);
+OPENREG_EXPORT orError_t orMemPoolTrim(size_t keep_bytes);
+
 /* Device */
 OPENREG_EXPORT orError_t orGetDeviceCount(int* count);
 OPENREG_EXPORT orError_t orSetDevice(int device);

@@ -26,6 +26,9 @@ SIGNATURES = {
     "orMemcpyAsync": (c_int, [c_void_p, c_void_p, ctypes.c_size_t, c_int, c_void_p]),
     "orPointerGetAttributes": (c_int, [c_void_p, c_void_p]),
     "orMemoryUnprotect": (c_int, [c_void_p]),
+    "orMallocAsync": (c_int, [ctypes.POINTER(c_void_p), ctypes.c_size_t, c_void_p]),
+    "orFreeAsync": (c_int, [c_void_p, c_void_p]),
+    "orMemPoolTrim": (c_int, [ctypes.c_size_t]),
     "orMemoryProtect": (c_int, [c_void_p]),
     "orGetDeviceCount": (c_int, [ctypes.POINTER(c_int)]),
     "orSetDevice": (c_int, [c_int]),
@@ -59,6 +62,13 @@ SIGNATURES = {
     "mcpu_gemm_swiglu": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int,
                                  c_void_p]),
     "mcpu_device_error": (c_int, [ctypes.POINTER(c_int), c_int]),
+    "mcpu_copy_strided": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p,
+                                  c_void_p]),
+    "mcpu_fill": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p, ctypes.c_double, c_int64, c_int,
+                          c_void_p]),
+    "mcpu_sigmoid": (c_int, [c_void_p, c_void_p, c_int64, c_int, c_void_p]),
+    "mcpu_silu": (c_int, [c_void_p, c_void_p, c_int64, c_int, c_void_p]),
+    "mcpu_mul": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_void_p]),
 }
 
 

@@ -1,0 +1,72 @@
+"""Builds the PyTorch-facing extension of the mcpu device in-tree.
+
+    python -m torch_mcpu_b200.build_ext   # -> torch_mcpu_b200/_ext_build/torch_mcpu_b200_C.so
+
+The extension (csrc_torch/*.cpp: PrivateUse1 allocator, guard, hooks, aten
+and mcpu:: registrations, the NCCL ProcessGroup, the Python methods) is a
+host-only layer over libtorch_mcpu_b200.so; it links that library with a
+relative rpath and NCCL from the PyTorch wheel.
+"""
+
+from __future__ import annotations
+
+import glob
+import os
+import sys
+
+from . import build as _cabi
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+SRC = os.path.join(HERE, "csrc_torch")
+OUT = os.path.join(HERE, "_ext_build")
+NAME = "torch_mcpu_b200_C"
+SO = os.path.join(OUT, NAME + ".so")
+
+
+def _nccl_dirs():
+    import nvidia.nccl as nccl  # the NCCL PyTorch itself loads
+
+    base = os.path.dirname(nccl.__file__) if getattr(nccl, "__file__", None) else list(nccl.__path__)[0]
+    return os.path.join(base, "include"), os.path.join(base, "lib")
+
+
+def sources():
+    return sorted(glob.glob(os.path.join(SRC, "*.cpp")))
+
+
+def up_to_date() -> bool:
+    if not os.path.exists(SO):
+        return False
+    deps = sources() + glob.glob(os.path.join(SRC, "*.h")) + glob.glob(os.path.join(ROOT, "include", "*.h"))
+    return os.path.getmtime(SO) >= max(os.path.getmtime(f) for f in deps)
+
+
+def build(verbose: bool = False) -> str:
+    _cabi.build()
+    if up_to_date():
+        return SO
+    from torch.utils import cpp_extension
+
+    nccl_inc, nccl_lib = _nccl_dirs()
+    cuda_inc = os.path.join(os.environ.get("CUDA_HOME", "/usr/local/cuda"), "include")
+    os.makedirs(OUT, exist_ok=True)
+    cpp_extension.load(
+        name=NAME,
+        sources=sources(),
+        build_directory=OUT,
+        extra_include_paths=[os.path.join(ROOT, "include"), SRC, nccl_inc, cuda_inc],
+        extra_cflags=["-O2", "-std=c++17", "-fvisibility=hidden"],
+        extra_ldflags=[
+            f"-L{HERE}", "-ltorch_mcpu_b200", "-Wl,-rpath,'$$ORIGIN/..'",
+            f"-L{nccl_lib}", "-l:libnccl.so.2", f"-Wl,-rpath,{nccl_lib}",
+        ],
+        with_cuda=False,
+        is_python_module=True,
+        verbose=verbose,
+    )
+    return SO
+
+
+if __name__ == "__main__":
+    print(build(verbose="-v" in sys.argv))
