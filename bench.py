@@ -12,7 +12,11 @@ timed with CUDA events on the launching stream, max over ranks.
 
 Multi-GPU: the router is independent per token, so N ranks run N replicas
 (weak scaling, no collective on the data path); `value` is all ranks'
-tokens over the slowest rank's time.
+tokens over the slowest rank's time.  The "tp_mlp" object reports the other
+half of the metric: the gated MLP H=4096 / I=14336 / T=2048 in bf16,
+tensor-parallel over the N ranks (TP=N), through the mcpu device (tcgen05
+GEMMs, fused SwiGLU) and its NCCL ProcessGroup (SUM all-reduce), in whole-job
+TFLOP/s over the slowest rank.
 
 --impl reference times the reference algorithm on the host cores (the
 oracle's C restatement of the reference's CPU path, all threads), rank 0
@@ -186,20 +190,24 @@ def cpu_baseline(seconds: float):
 def dist_setup(n):
     import torch
 
+    import torch_mcpu_b200.device  # noqa: F401  the mcpu device + its NCCL ProcessGroup
+
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if world != n:
         raise SystemExit(f"--gpus {n} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    torch.mcpu.set_device(local)
     pg = None
     if world > 1:
         import datetime
 
         import torch.distributed as dist
 
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
+        # the reference's init string: gloo for CPU tensors, the mcpu backend
+        # (NCCL over NVLink here) for mcpu tensors
+        dist.init_process_group("cpu:gloo,mcpu:mcpu", timeout=datetime.timedelta(seconds=120))
         pg = dist
     return rank, world, local, pg
 
@@ -209,14 +217,74 @@ def barrier(pg):
         pg.barrier()
 
 
-def max_over_ranks(pg, v: float, dev) -> float:
+def max_over_ranks(pg, v: float, dev=None) -> float:
     if pg is None:
         return v
     import torch
 
-    t = torch.tensor([v], dtype=torch.float64, device=dev)
+    t = torch.tensor([v], dtype=torch.float64)
     pg.all_reduce(t, op=pg.ReduceOp.MAX)
     return float(t.item())
+
+
+# ---------------------------------------------------------------- TP MLP
+def tp_mlp_leg(rank, world, pg, steps, warmup):
+    """Gated MLP H=4096, I=14336, T=2048 (bf16), tensor-parallel over the
+    N ranks: fused gate/up GEMM + SwiGLU, down GEMM, SUM all-reduce of the
+    partial outputs through the mcpu ProcessGroup (NCCL).  Whole-job TFLOP/s
+    over the slowest rank's CUDA-event time."""
+    import torch
+
+    import configs as C
+
+    cfg = C.MLP_M1
+    x, _, wgu, wd = C.mlp_weights(cfg, world, rank)
+    from torch_mcpu_b200 import ops
+
+    xm = x.to("mcpu")
+    wgu_il = ops.interleave_gate_up(wgu).to("mcpu")
+    wdm = wd.to("mcpu")
+
+    def step():
+        act = torch.ops.mcpu.gemm_swiglu(xm, wgu_il)
+        y = torch.mm(act, wdm.t())
+        if pg is not None:
+            pg.all_reduce(y)
+        return y
+
+    for _ in range(max(3, warmup)):
+        step()
+    torch.mcpu.synchronize()
+    barrier(pg)
+    e0 = torch.Event(device="mcpu", enable_timing=True)
+    e1 = torch.Event(device="mcpu", enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        step()
+    e1.record()
+    e1.synchronize()
+    ms = max_over_ranks(pg, e0.elapsed_time(e1)) / steps
+    flops = 2 * cfg.T * cfg.H * cfg.I * 3
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            pk = json.load(f)
+        peaks = {"bf16_tflops": pk["bf16_tflops"], "bf16_tflops_sustained": pk["bf16_tflops_sustained"]}
+    except Exception:
+        peaks = {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "kind": "fallback"}
+    whole = flops / (ms * 1e-3) / 1e12
+    per_gpu = whole / world
+    return {
+        "config": f"gated MLP bf16 H={cfg.H} I={cfg.I} T={cfg.T} TP={world} (gate/up column-parallel, "
+                  "down row-parallel, SUM all-reduce over the mcpu ProcessGroup)",
+        "tflops": round(whole, 1),
+        "per_gpu_tflops": round(per_gpu, 1),
+        "ms_per_step": round(ms, 4),
+        "frac_of_bf16_peak": round(per_gpu / peaks["bf16_tflops"], 4),
+        "frac_of_bf16_sustained": round(per_gpu / peaks["bf16_tflops_sustained"], 4),
+        "steps": steps,
+        "flops_per_step": flops,
+    }
 
 
 # ---------------------------------------------------------------- ours
@@ -229,7 +297,6 @@ def run_ours(a):
 
     rank, world, local, pg = dist_setup(a.gpus)
     dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
     lib = _lib.load()
 
     cfg = C.deepseek_v3(T)
@@ -295,7 +362,7 @@ def run_ours(a):
     torch.cuda.synchronize(dev)
     barrier(pg)
     ms = ev0.elapsed_time(ev1)
-    ms_max = max_over_ranks(pg, ms, dev)
+    ms_max = max_over_ranks(pg, ms)
     exact = ctypes.c_ulonglong(0)
     lib.mcpu_grouped_topk_exact_rows(ctypes.byref(exact), 0)
     exact_per_step = exact.value / (steps + reps_w * GRAPH_STEPS)
@@ -330,7 +397,9 @@ def run_ours(a):
         ev1.record(stream)
     ev1.synchronize()
     barrier(pg)
-    e2e_ms = max_over_ranks(pg, ev0.elapsed_time(ev1), dev) / e2e_steps
+    e2e_ms = max_over_ranks(pg, ev0.elapsed_time(ev1)) / e2e_steps
+    del graph
+    mlp = tp_mlp_leg(rank, world, pg, steps=max(10, min(a.steps, 50)), warmup=3)
 
     if rank == 0:
         per_step = ms_max / steps
@@ -371,10 +440,10 @@ def run_ours(a):
             "clocks": clk.summary(),
             "gpu_launches": steps,
             "exact_path_rows_per_step": round(exact_per_step, 2),
+            "tp_mlp": mlp,
         }
         line["cpu_baseline"] = cpu_baseline(a.cpu_seconds) if world == 1 else None
         print(json.dumps(line), flush=True)
-    del graph
     if pg is not None:
         pg.destroy_process_group()
 
