@@ -164,3 +164,19 @@ def test_rms_norm_zero_rows_and_large_values():
     x[1] = x[1] * 1e30
     out = run_rms(x, w, C.RMS_EPS)
     np.testing.assert_array_equal(bits(out), oracle.rms_norm_bf16(bits(x), bits(w), C.RMS_EPS))
+
+
+def test_elementwise_sigmoid_silu_on_a_strided_sample_of_all_fp32():
+    """The device's correctly rounded exp (fp32 arithmetic only) against the
+    oracle's (float)exp((double)x) on every 97th fp32 bit pattern."""
+    u = np.arange(0, 1 << 32, 97, dtype=np.uint64).astype(np.uint32)
+    x = u.view(np.float32)
+    x = x[np.isfinite(x)]
+    xd = torch.from_numpy(x).to(DEV)
+    s = _m().sigmoid(xd).cpu().numpy()
+    t = _m().silu(xd).cpu().numpy()
+    ref_s = oracle.sigmoid_f32(x, oracle.EXP_CR)
+    np.testing.assert_array_equal(s.view(np.uint32), ref_s.view(np.uint32))
+    ref_t = (x / (np.float32(1.0) + np.exp(-x.astype(np.float64)).astype(np.float32))).astype(np.float32)
+    ok = ~(np.isnan(t) & np.isnan(ref_t))
+    np.testing.assert_array_equal(t.view(np.uint32)[ok], ref_t.view(np.uint32)[ok])

@@ -14,8 +14,10 @@ from .ops import (  # noqa: F401
     interleave_gate_up,
     mm_nt,
     rms_norm,
+    sigmoid,
+    silu,
     silu_and_mul,
 )
 
 __all__ = ["grouped_topk", "grouped_topk_exact_rows", "silu_and_mul", "rms_norm", "mm_nt",
-           "gemm_swiglu", "interleave_gate_up", "device_error"]
+           "gemm_swiglu", "interleave_gate_up", "device_error", "sigmoid", "silu"]

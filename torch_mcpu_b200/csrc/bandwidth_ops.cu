@@ -10,8 +10,8 @@
 //   rounding can depend on how exp is evaluated.  The kernel evaluates silu
 //   with ex2.approx/rcp.approx and, when the fp32 result lies within its
 //   error bound of a bf16 rounding midpoint (about 1e-4 of elements) or |a|
-//   is large, re-evaluates it with a correctly rounded exp; the bf16 result
-//   therefore equals the reference formula's.
+//   is large, re-evaluates it with the correctly rounded exp of expf_cr.h;
+//   the bf16 result therefore equals the reference formula's.
 //
 // rms_norm: vLLM rms_norm native (vllm/ir/ops/layernorm.py:14-21) on bf16:
 //   var = mean(float(x)^2); y = bf16(float(x) * (1 / sqrt(var + eps)));
@@ -22,6 +22,7 @@
 #include <math.h>
 
 #include "common.cuh"
+#include "expf_cr.h"
 
 namespace mcpu {
 namespace bw {
@@ -38,10 +39,7 @@ __device__ __forceinline__ float rcp_approx(float y) {
   return r;
 }
 
-__device__ __forceinline__ float silu_exact(float a) {
-  const float e = static_cast<float>(exp(-static_cast<double>(a)));
-  return __fdiv_rn(a, __fadd_rn(1.0f, e));
-}
+__device__ __noinline__ float silu_exact(float a) { return crexp::silu_cr(a); }
 
 // bf16(silu(a)) as the reference computes it.
 __device__ __forceinline__ float silu_bf16(float a) {

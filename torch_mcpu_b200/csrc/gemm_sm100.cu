@@ -28,6 +28,7 @@
 
 #include "common.cuh"
 #include "sm100.cuh"
+#include "expf_cr.h"
 
 namespace mcpu {
 namespace gemm {
@@ -70,6 +71,8 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
          (static_cast<uint32_t>(float_to_bf16_bits(hi)) << 16);
 }
 
+__device__ __noinline__ float silu_slow(float a) { return crexp::silu_cr(a); }
+
 // bf16(silu(g)) with the reference's formula g / (1 + exp(-g)) and a
 // correctly rounded exp wherever the fast value is near a bf16 midpoint.
 __device__ __forceinline__ float silu_bf16_exact(float a) {
@@ -83,8 +86,7 @@ __device__ __forceinline__ float silu_bf16_exact(float a) {
     const int window = 32 + 4 * static_cast<int>(aa + 1.0f);
     if (abs(low) > window && s != 0.0f) return round_bf16(s);
   }
-  const float e = static_cast<float>(exp(-static_cast<double>(a)));
-  return round_bf16(__fdiv_rn(a, __fadd_rn(1.0f, e)));
+  return round_bf16(silu_slow(a));
 }
 
 __global__ void __launch_bounds__(THREADS, 1)

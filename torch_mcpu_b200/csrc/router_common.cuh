@@ -5,6 +5,7 @@
 #include <math.h>
 
 #include "common.cuh"
+#include "expf_cr.h"
 
 namespace mcpu {
 namespace router {
@@ -32,16 +33,12 @@ __device__ __forceinline__ float sigmoid_fast(float x) {
   return rcp_approx(__fadd_rn(1.0f, e));
 }
 
-// The reference formula with exp correctly rounded to fp32:
-// (float)exp((double)y) rounds correctly for every fp32 y (checked
-// exhaustively against an extended-precision exp on the host).
-__device__ __forceinline__ float sigmoid_exact(float x) {
-  const float e = static_cast<float>(exp(-static_cast<double>(x)));
-  return __fdiv_rn(1.0f, __fadd_rn(1.0f, e));
-}
+// The reference formula 1.0f / (1.0f + expf(-x)) with exp correctly
+// rounded (fp32 arithmetic only, see expf_cr.h).
+__device__ __forceinline__ float sigmoid_exact(float x) { return crexp::sigmoid_cr(x); }
 
-// Out-of-line copy for the rare exact paths: keeps the compiler from
-// interleaving dozens of fp64 exp evaluations (and their registers).
+// Out-of-line copy for the rare exact paths: keeps their code and registers
+// out of the unrolled fast paths.
 __device__ __noinline__ float sigmoid_exact_call(float x) { return sigmoid_exact(x); }
 
 __device__ __forceinline__ float fast_key(float x, float b) {

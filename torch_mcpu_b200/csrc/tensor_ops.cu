@@ -17,6 +17,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "expf_cr.h"
 
 namespace mcpu {
 namespace tensor {
@@ -103,13 +104,36 @@ __device__ __forceinline__ void offsets(const Strided& s, long long lin, long lo
   *dof = b;
 }
 
+template <int DT>
+constexpr bool is_f32_family() {
+  return DT == MCPU_FLOAT32 || DT == MCPU_BFLOAT16 || DT == MCPU_FLOAT16;
+}
+
+template <int DT>
+__device__ __forceinline__ float load_f(const void* p, long long off) {
+  if constexpr (DT == MCPU_FLOAT32) return static_cast<const float*>(p)[off];
+  else if constexpr (DT == MCPU_BFLOAT16) return bf16_bits_to_float(static_cast<const uint16_t*>(p)[off]);
+  else return __half2float(static_cast<const __half*>(p)[off]);
+}
+
+template <int DT>
+__device__ __forceinline__ void store_f(void* p, long long off, float v) {
+  if constexpr (DT == MCPU_FLOAT32) static_cast<float*>(p)[off] = v;
+  else if constexpr (DT == MCPU_BFLOAT16) static_cast<uint16_t*>(p)[off] = float_to_bf16_bits(v);
+  else static_cast<__half*>(p)[off] = __float2half_rn(v);
+}
+
 template <int SDT, int DDT>
 __global__ void copy_kernel(const void* src, void* dst, const Strided s, long long n) {
   for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
     long long so, dof;
     offsets(s, i, &so, &dof);
-    store<DDT>(dst, dof, load<SDT>(src, so));
+    if constexpr (is_f32_family<SDT>() && is_f32_family<DDT>()) {
+      store_f<DDT>(dst, dof, load_f<SDT>(src, so));  // fp32 <-> bf16 / fp16 without fp64
+    } else {
+      store<DDT>(dst, dof, load<SDT>(src, so));
+    }
   }
 }
 
@@ -169,7 +193,6 @@ static int grid_for(long long n) {
 }
 
 // ---------------------------------------------------------------- elementwise
-__device__ __forceinline__ float exp_cr(float y) { return static_cast<float>(exp(static_cast<double>(y))); }
 
 template <int DT>
 __global__ void sigmoid_kernel(const void* x, void* out, long long n) {
@@ -178,7 +201,7 @@ __global__ void sigmoid_kernel(const void* x, void* out, long long n) {
     float v;
     if constexpr (DT == MCPU_FLOAT32) v = static_cast<const float*>(x)[i];
     else v = bf16_bits_to_float(static_cast<const uint16_t*>(x)[i]);
-    const float s = __fdiv_rn(1.0f, __fadd_rn(1.0f, exp_cr(-v)));
+    const float s = crexp::sigmoid_cr(v);
     if constexpr (DT == MCPU_FLOAT32) static_cast<float*>(out)[i] = s;
     else static_cast<uint16_t*>(out)[i] = float_to_bf16_bits(s);
   }
@@ -191,7 +214,7 @@ __global__ void silu_kernel(const void* x, void* out, long long n) {
     float v;
     if constexpr (DT == MCPU_FLOAT32) v = static_cast<const float*>(x)[i];
     else v = bf16_bits_to_float(static_cast<const uint16_t*>(x)[i]);
-    const float s = __fdiv_rn(v, __fadd_rn(1.0f, exp_cr(-v)));
+    const float s = crexp::silu_cr(v);
     if constexpr (DT == MCPU_FLOAT32) static_cast<float*>(out)[i] = s;
     else static_cast<uint16_t*>(out)[i] = float_to_bf16_bits(s);
   }

@@ -69,6 +69,15 @@ static thread_local std::array<int64_t, kMaxDevices> tl_current = [] {
   return a;
 }();
 
+c10::DeviceIndex current_device();
+
+// A device given without an index ("mcpu") means the current device.
+static c10::DeviceIndex norm_index(c10::DeviceIndex d) {
+  if (d < 0) d = current_device();
+  TORCH_CHECK(d >= 0 && d < kMaxDevices, "mcpu: device index ", static_cast<int>(d), " out of range");
+  return d;
+}
+
 static orStream_t create_stream(int priority) {
   orStream_t s = nullptr;
   MCPU_TORCH_CHECK(orStreamCreateWithPriority(&s, orStreamDefault, priority), "orStreamCreateWithPriority");
@@ -76,6 +85,7 @@ static orStream_t create_stream(int priority) {
 }
 
 static void ensure_default(c10::DeviceIndex dev) {
+  dev = norm_index(dev);
   auto& t = table();
   std::lock_guard<std::mutex> g(t.mu);
   if (t.streams[dev].empty()) {
@@ -88,7 +98,7 @@ static void ensure_default(c10::DeviceIndex dev) {
 }
 
 orStream_t stream_handle(const c10::Stream& s) {
-  const c10::DeviceIndex dev = s.device_index();
+  const c10::DeviceIndex dev = norm_index(s.device_index());
   ensure_default(dev);
   auto& t = table();
   std::lock_guard<std::mutex> g(t.mu);
@@ -104,7 +114,7 @@ c10::DeviceIndex current_device() {
 }
 
 c10::Stream current_stream(c10::DeviceIndex dev) {
-  if (dev < 0) dev = current_device();
+  dev = norm_index(dev);
   ensure_default(dev);
   return c10::Stream(c10::Stream::UNSAFE, c10::Device(c10::DeviceType::PrivateUse1, dev), tl_current[dev]);
 }
@@ -112,6 +122,7 @@ c10::Stream current_stream(c10::DeviceIndex dev) {
 orStream_t current_stream_handle(c10::DeviceIndex dev) { return stream_handle(current_stream(dev)); }
 
 static c10::Stream new_stream(c10::DeviceIndex dev, int priority) {
+  dev = norm_index(dev);
   ensure_default(dev);
   int prev = 0;
   orGetDevice(&prev);
@@ -125,7 +136,7 @@ static c10::Stream new_stream(c10::DeviceIndex dev, int priority) {
                      static_cast<int64_t>(t.streams[dev].size() - 1));
 }
 
-static void set_current_stream(const c10::Stream& s) { tl_current[s.device_index()] = s.id(); }
+static void set_current_stream(const c10::Stream& s) { tl_current[norm_index(s.device_index())] = s.id(); }
 
 // ------------------------------------------------------------------ allocator
 struct Block {
@@ -228,19 +239,24 @@ struct McpuGuardImpl final : c10::impl::DeviceGuardImplInterface {
     return old;
   }
   c10::Device getDevice() const override { return c10::Device(static_type, current_device()); }
-  void setDevice(c10::Device d) const override { MCPU_TORCH_CHECK(orSetDevice(d.index()), "orSetDevice"); }
-  void uncheckedSetDevice(c10::Device d) const noexcept override { orSetDevice(d.index()); }
+  void setDevice(c10::Device d) const override {
+    if (d.index() >= 0) MCPU_TORCH_CHECK(orSetDevice(d.index()), "orSetDevice");
+  }
+  void uncheckedSetDevice(c10::Device d) const noexcept override {
+    if (d.index() >= 0) orSetDevice(d.index());
+  }
   c10::Stream getStream(c10::Device d) const override { return current_stream(d.index()); }
   c10::Stream getDefaultStream(c10::Device d) const override {
-    ensure_default(d.index());
-    return c10::Stream(c10::Stream::UNSAFE, d, 0);
+    const c10::DeviceIndex i = norm_index(d.index());
+    ensure_default(i);
+    return c10::Stream(c10::Stream::UNSAFE, c10::Device(static_type, i), 0);
   }
   c10::Stream getNewStream(c10::Device d, int priority) const override { return new_stream(d.index(), priority); }
   c10::Stream getStreamFromGlobalPool(c10::Device d, bool high) const override {
     return new_stream(d.index(), high ? -1 : 0);
   }
   c10::Stream exchangeStream(c10::Stream s) const override {
-    const c10::Stream old = current_stream(s.device_index());
+    const c10::Stream old = current_stream(norm_index(s.device_index()));
     set_current_stream(s);
     return old;
   }
@@ -251,7 +267,7 @@ struct McpuGuardImpl final : c10::impl::DeviceGuardImplInterface {
   }
   void record(void** event, const c10::Stream& stream, const c10::DeviceIndex device_index,
               const c10::EventFlag flag) const override {
-    TORCH_CHECK(device_index == -1 || device_index == stream.device_index(),
+    TORCH_CHECK(device_index == -1 || stream.device_index() == -1 || device_index == stream.device_index(),
                 "event device does not match the stream's device");
     if (!*event) {
       orEvent_t e = nullptr;

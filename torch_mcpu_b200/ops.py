@@ -185,3 +185,25 @@ def device_error(reset: bool = False) -> int:
     f = ctypes.c_int(0)
     _lib.check(_lib.load().mcpu_device_error(ctypes.byref(f), int(reset)), "device_error")
     return int(f.value)
+
+
+def _elementwise(fn_name: str, x: torch.Tensor) -> torch.Tensor:
+    _require_device(x, "x")
+    if x.dtype not in (torch.float32, torch.bfloat16):
+        raise RuntimeError(f"{fn_name}: float32 or bfloat16 only")
+    x = x.contiguous()
+    out = torch.empty_like(x)
+    fn = getattr(_lib.load(), "mcpu_" + fn_name)
+    _lib.check(fn(out.data_ptr(), x.data_ptr(), x.numel(), _DTYPES[x.dtype], _stream_handle(x.device)), fn_name)
+    return out
+
+
+def sigmoid(x: torch.Tensor) -> torch.Tensor:
+    """1 / (1 + exp(-x)) with exp correctly rounded: the reference's raw
+    sigmoid loop (csrc/aten/ops/unary_out.cpp:46-49)."""
+    return _elementwise("sigmoid", x)
+
+
+def silu(x: torch.Tensor) -> torch.Tensor:
+    """x / (1 + exp(-x)) with exp correctly rounded (unary_out.cpp:50-51)."""
+    return _elementwise("silu", x)
