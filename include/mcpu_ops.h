@@ -145,11 +145,22 @@ OPENREG_EXPORT orError_t mcpu_gemm_swiglu(const void* x, const void* w_gate_up, 
                                           int64_t M, int64_t I, int64_t K, int dtype,
                                           orStream_t stream);
 
-/* *flag = 1 if a kernel on the current device (tensor-core GEMM or TMA-fed
- * router) gave up on a bounded wait since the last reset; that launch left
+/* *flag = 1 if a kernel on the current device (tensor-core GEMM, TMA-fed
+ * router or bulk-copy-fed rms_norm) gave up on a bounded wait since the last
+ * reset; that launch left
  * its output incomplete.  No counterpart in the reference, whose host
  * worker threads report hangs through orStreamSynchronize's timeout. */
 OPENREG_EXPORT orError_t mcpu_device_error(int* flag, int reset);
+
+/* Free and total device memory of `device` (cudaMemGetInfo).  Backs
+ * torch.mcpu.mem_get_info (torch_mcpu/openreg/__init__.py:391-395 of the
+ * reference, where it reports the simulated device's memory). */
+OPENREG_EXPORT orError_t mcpu_mem_get_info(int device, size_t* free_bytes, size_t* total_bytes);
+
+/* Bytes reserved by the stream-ordered pool behind orMallocAsync on `device`
+ * (current and high-water mark).  Backs torch.mcpu.memory_reserved /
+ * max_memory_reserved (reference: the caching allocator's reserved bytes). */
+OPENREG_EXPORT orError_t mcpu_mem_pool_reserved(int device, uint64_t* current, uint64_t* peak);
 
 /*
  * Tensor plumbing of the mcpu device (all asynchronous on `stream`).

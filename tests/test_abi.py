@@ -71,3 +71,22 @@ def test_memory_protection_calls_are_accepted():
 
     lib = _lib.load()
     assert lib.orMemoryProtect(None) == 0 and lib.orMemoryUnprotect(None) == 0
+
+
+def test_extension_exports_the_launch_api():
+    """include/mcpu_launch.h's exported functions (kernel timing, guards,
+    stream lookups) are defined by the PyTorch-facing extension."""
+    import subprocess
+
+    from torch_mcpu_b200 import build_ext
+
+    if not os.path.exists(build_ext.SO):
+        pytest.skip("extension not built")
+    src = open(os.path.join(ROOT, "include", "mcpu_launch.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    src = "\n".join(line for line in src.splitlines() if not line.lstrip().startswith("#"))
+    wanted = set(re.findall(r"MCPU_LAUNCH_EXPORT\s+(?:extern\s+)?[\w:<>\s\*&]*?\b(\w+)\s*[\(;]", src))
+    assert {"getCurrentMcpuStream", "reserve_event_slot", "get_kernel_launch_stream", "g_enabled"} <= wanted
+    out = subprocess.run(["nm", "-DC", "--defined-only", build_ext.SO], capture_output=True, text=True).stdout
+    missing = [w for w in wanted if not re.search(r"\b" + w + r"\b", out)]
+    assert not missing, missing

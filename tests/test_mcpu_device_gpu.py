@@ -125,3 +125,16 @@ def test_memory_stats_track_allocations(mcpu):
     del t
     assert torch.mcpu.memory_allocated() == base
     torch.mcpu.empty_cache()
+
+
+def test_device_module_api(mcpu):
+    free, total = torch.mcpu.mem_get_info()
+    assert 0 < free <= total
+    with torch.mcpu.device(0):
+        assert torch.mcpu.current_device() == 0
+    t = torch.empty(1 << 20, device="mcpu")
+    assert torch.mcpu.memory_reserved() >= 4 << 20
+    assert torch.mcpu.max_memory_reserved() >= torch.mcpu.memory_reserved()
+    del t
+    d = torch.mcpu.default_stream()
+    assert d.device_type == torch.device("mcpu").type or d.device.type == "mcpu"

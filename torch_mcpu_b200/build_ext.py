@@ -68,5 +68,37 @@ def build(verbose: bool = False) -> str:
     return SO
 
 
+CHECK_SRC = os.path.join(ROOT, "tests", "launch_api", "launch_check.cu")
+CHECK_NAME = "mcpu_launch_check"
+CHECK_SO = os.path.join(OUT, CHECK_NAME + ".so")
+
+
+def build_launch_check(verbose: bool = False) -> str:
+    """The launch-API caller used by tests/test_launch_api_gpu.py: compiled
+    by nvcc for sm_100a against include/mcpu_launch.h, linked to the
+    extension that exports the API's functions."""
+    build()
+    deps = [CHECK_SRC, SO, os.path.join(ROOT, "include", "mcpu_launch.h")]
+    if os.path.exists(CHECK_SO) and os.path.getmtime(CHECK_SO) >= max(os.path.getmtime(f) for f in deps):
+        return CHECK_SO
+    from torch.utils import cpp_extension
+
+    cpp_extension.load(
+        name=CHECK_NAME,
+        sources=[CHECK_SRC],
+        build_directory=OUT,
+        extra_include_paths=[os.path.join(ROOT, "include")],
+        extra_cflags=["-O2", "-std=c++17"],
+        extra_cuda_cflags=["-O2", "-std=c++17", "-gencode", "arch=compute_100a,code=sm_100a"],
+        extra_ldflags=[f"-L{OUT}", f"-l:{NAME}.so", "-Wl,-rpath,'$$ORIGIN'"],
+        with_cuda=True,
+        is_python_module=True,
+        verbose=verbose,
+    )
+    return CHECK_SO
+
+
 if __name__ == "__main__":
     print(build(verbose="-v" in sys.argv))
+    if "--launch-check" in sys.argv:
+        print(build_launch_check(verbose="-v" in sys.argv))

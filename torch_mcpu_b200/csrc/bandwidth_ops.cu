@@ -23,6 +23,7 @@
 
 #include "common.cuh"
 #include "expf_cr.h"
+#include "sm100.cuh"
 
 namespace mcpu {
 namespace bw {
@@ -80,39 +81,60 @@ __device__ __forceinline__ void stg_stream(uint4* p, uint4 v) {
 }
 
 // 8 outputs (16 bytes) per vector; d % 8 == 0 and 16-byte aligned rows.
-__global__ void __launch_bounds__(256) silu_and_mul_vec_kernel(const uint4* __restrict__ x,
-                                                              uint4* __restrict__ out,
-                                                              long long T, long long dv) {
+// CTAs loop over rows, so no index division; each thread keeps three
+// vector pairs in flight.
+__global__ void __launch_bounds__(256) silu_and_mul_rows_kernel(const uint4* __restrict__ x,
+                                                               uint4* __restrict__ out,
+                                                               long long T, int dv) {
+  for (long long t = blockIdx.x; t < T; t += gridDim.x) {
+    const uint4* a = x + t * 2 * dv;
+    const uint4* b = a + dv;
+    uint4* o = out + t * dv;
+    int j = threadIdx.x;
+    for (; j + 2 * 256 < dv; j += 3 * 256) {
+      uint4 av[3], bv[3];
+#pragma unroll
+      for (int u = 0; u < 3; ++u) {
+        av[u] = ldg_stream(a + j + u * 256);
+        bv[u] = ldg_stream(b + j + u * 256);
+      }
+#pragma unroll
+      for (int u = 0; u < 3; ++u) {
+        uint4 r;
+        r.x = silu_mul_pair(av[u].x, bv[u].x);
+        r.y = silu_mul_pair(av[u].y, bv[u].y);
+        r.z = silu_mul_pair(av[u].z, bv[u].z);
+        r.w = silu_mul_pair(av[u].w, bv[u].w);
+        stg_stream(o + j + u * 256, r);
+      }
+    }
+    for (; j < dv; j += 256) {
+      const uint4 av = ldg_stream(a + j), bv = ldg_stream(b + j);
+      uint4 r;
+      r.x = silu_mul_pair(av.x, bv.x);
+      r.y = silu_mul_pair(av.y, bv.y);
+      r.z = silu_mul_pair(av.z, bv.z);
+      r.w = silu_mul_pair(av.w, bv.w);
+      stg_stream(o + j, r);
+    }
+  }
+}
+
+// Narrow rows (fewer than 256 vectors): one flat index space.
+__global__ void __launch_bounds__(256) silu_and_mul_flat_kernel(const uint4* __restrict__ x,
+                                                               uint4* __restrict__ out,
+                                                               long long T, long long dv) {
   const long long total = T * dv;
-  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
   for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
-       i += 2 * stride) {
-    const long long i2 = i + stride;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
     const long long t = i / dv, j = i - t * dv;
-    const uint4 a = ldg_stream(x + t * 2 * dv + j);
-    const uint4 b = ldg_stream(x + t * 2 * dv + dv + j);
-    uint4 a2 = make_uint4(0, 0, 0, 0), b2 = a2;
-    long long t2 = 0, j2 = 0;
-    if (i2 < total) {
-      t2 = i2 / dv;
-      j2 = i2 - t2 * dv;
-      a2 = ldg_stream(x + t2 * 2 * dv + j2);
-      b2 = ldg_stream(x + t2 * 2 * dv + dv + j2);
-    }
-    uint4 o;
-    o.x = silu_mul_pair(a.x, b.x);
-    o.y = silu_mul_pair(a.y, b.y);
-    o.z = silu_mul_pair(a.z, b.z);
-    o.w = silu_mul_pair(a.w, b.w);
-    stg_stream(out + t * dv + j, o);
-    if (i2 < total) {
-      uint4 o2;
-      o2.x = silu_mul_pair(a2.x, b2.x);
-      o2.y = silu_mul_pair(a2.y, b2.y);
-      o2.z = silu_mul_pair(a2.z, b2.z);
-      o2.w = silu_mul_pair(a2.w, b2.w);
-      stg_stream(out + t2 * dv + j2, o2);
-    }
+    const uint4 av = ldg_stream(x + t * 2 * dv + j), bv = ldg_stream(x + t * 2 * dv + dv + j);
+    uint4 r;
+    r.x = silu_mul_pair(av.x, bv.x);
+    r.y = silu_mul_pair(av.y, bv.y);
+    r.z = silu_mul_pair(av.z, bv.z);
+    r.w = silu_mul_pair(av.w, bv.w);
+    stg_stream(out + i, r);
   }
 }
 
@@ -130,17 +152,22 @@ __global__ void silu_and_mul_scalar_kernel(const uint16_t* __restrict__ x, uint1
 
 // ------------------------------------------------------------------ rms_norm
 constexpr int kRmsThreads = 256;
-constexpr int kRmsMaxVec = 8;  // vectors of 8 bf16 per thread: H <= 16384
 
-__device__ __forceinline__ double block_sum(double v, double* smem) {
+__device__ int g_bw_error = 0;
+
+// Sum over the CTA in a fixed order (identical in every thread).  The
+// barrier also ORs `fail` over the CTA into *any_fail.
+__device__ __forceinline__ double block_sum(double v, double* smem, bool fail = false,
+                                           bool* any_fail = nullptr) {
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, off);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (lane == 0) smem[warp] = v;
-  __syncthreads();
+  const int f = __syncthreads_or(fail ? 1 : 0);
+  if (any_fail) *any_fail = f != 0;
   double r = 0.0;
   const int nw = blockDim.x >> 5;
-  for (int i = 0; i < nw; ++i) r += smem[i];  // same order in every thread
+  for (int i = 0; i < nw; ++i) r += smem[i];
   return r;
 }
 
@@ -149,46 +176,102 @@ __device__ __forceinline__ float normed(float v, float r, float w) {
   return __fmul_rn(y, w);
 }
 
-__global__ void __launch_bounds__(kRmsThreads) rms_norm_vec_kernel(
-    const uint4* __restrict__ x, const uint4* __restrict__ w, uint4* __restrict__ out, int hv,
-    double count, float eps) {
-  __shared__ double red[kRmsThreads / 32];
-  const long long row = blockIdx.x;
-  const uint4* xr = x + row * hv;
-  uint4 v[kRmsMaxVec];
-  double acc = 0.0;
-#pragma unroll
-  for (int k = 0; k < kRmsMaxVec; ++k) {
-    const int c = threadIdx.x + k * kRmsThreads;
-    v[k] = c < hv ? ldg_stream(xr + c) : make_uint4(0, 0, 0, 0);
-    const uint32_t q[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float lo = __uint_as_float(q[e] << 16), hi = __uint_as_float(q[e] & 0xFFFF0000u);
-      acc += static_cast<double>(__fmul_rn(lo, lo));
-      acc += static_cast<double>(__fmul_rn(hi, hi));
+// Persistent CTAs; rows stream through a ring of `stages` shared-memory row
+// buffers filled by bulk copies (one mbarrier per buffer), so the next rows
+// are in flight while this one is reduced.  Each thread owns the vectors
+// c = threadIdx.x + k * 256 of a row and of the weight.
+// Rows are 16-byte multiples (H % 8 == 0) and 16-byte aligned.
+template <int NV>
+__global__ void __launch_bounds__(kRmsThreads, NV <= 4 ? 4 : 1) rms_norm_ring_kernel(
+    const uint8_t* __restrict__ x, const uint4* __restrict__ w, uint4* __restrict__ out, int hv,
+    long long T, int stages, double count, float eps) {
+  extern __shared__ __align__(128) uint8_t ring[];
+  const int row_bytes = hv * 16;
+  const int slot = (row_bytes + 127) & ~127;
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + stages * slot);
+  double* red = reinterpret_cast<double*>(full + stages);  // [2][kRmsThreads / 32]
+  int* abort_flag = reinterpret_cast<int*>(red + 2 * (kRmsThreads / 32));
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) sm100::mbar_init(&full[s], 1);
+    *abort_flag = 0;
+    sm100::fence_barrier_init();
+    for (int s = 0; s < stages; ++s) {
+      const long long row = blockIdx.x + static_cast<long long>(s) * gridDim.x;
+      if (row < T) {
+        sm100::mbar_arrive_expect_tx(&full[s], row_bytes);
+        sm100::bulk_load(ring + s * slot, x + row * row_bytes, row_bytes, &full[s]);
+      }
     }
   }
-  const double total = block_sum(acc, red);
-  const float var = static_cast<float>(total / count);
-  const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
-  uint4* orow = out + row * hv;
+  __syncthreads();
+
+  int i = 0;
+  for (;; ++i) {
+    const long long row = blockIdx.x + static_cast<long long>(i) * gridDim.x;
+    if (row >= T) break;
+    const int st = i % stages;
+    const bool ok = sm100::mbar_wait(&full[st], (i / stages) & 1, abort_flag);
+    const uint4* src = reinterpret_cast<const uint4*>(ring + st * slot);
+    uint4 v[NV];
+    double acc = 0.0;
 #pragma unroll
-  for (int k = 0; k < kRmsMaxVec; ++k) {
-    const int c = threadIdx.x + k * kRmsThreads;
-    if (c < hv) {
-      const uint4 wv = __ldg(w + c);
+    for (int k = 0; k < NV; ++k) {
+      const int c = threadIdx.x + k * kRmsThreads;
+      v[k] = (ok && c < hv) ? src[c] : make_uint4(0, 0, 0, 0);
       const uint32_t q[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
-      const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
-      uint32_t o[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const float lo = normed(__uint_as_float(q[e] << 16), r, __uint_as_float(ww[e] << 16));
-        const float hi = normed(__uint_as_float(q[e] & 0xFFFF0000u), r,
-                                __uint_as_float(ww[e] & 0xFFFF0000u));
-        o[e] = float_to_bf16_bits(lo) | (static_cast<uint32_t>(float_to_bf16_bits(hi)) << 16);
+        const float lo = __uint_as_float(q[e] << 16), hi = __uint_as_float(q[e] & 0xFFFF0000u);
+        acc += static_cast<double>(__fmul_rn(lo, lo));
+        acc += static_cast<double>(__fmul_rn(hi, hi));
       }
-      stg_stream(orow + c, make_uint4(o[0], o[1], o[2], o[3]));
+    }
+    // after this barrier every thread has read buffer st: refill it (or
+    // leave together when any thread's wait gave up)
+    bool failed = false;
+    const double total = block_sum(acc, red + (i & 1) * (kRmsThreads / 32), !ok, &failed);
+    if (failed) {
+      if (threadIdx.x == 0) *abort_flag = 1;
+      break;
+    }
+    if (threadIdx.x == 0) {
+      const long long nrow = row + static_cast<long long>(stages) * gridDim.x;
+      if (nrow < T) {
+        sm100::mbar_arrive_expect_tx(&full[st], row_bytes);
+        sm100::bulk_load(ring + st * slot, x + nrow * row_bytes, row_bytes, &full[st]);
+      }
+    }
+    const float var = static_cast<float>(total / count);
+    const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+    uint4* orow = out + row * hv;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      const int c = threadIdx.x + k * kRmsThreads;
+      if (c < hv) {
+        const uint4 wv = __ldg(w + c);  // 2H bytes, L1-resident across rows
+        const uint32_t q[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+        const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float lo = normed(__uint_as_float(q[e] << 16), r, __uint_as_float(ww[e] << 16));
+          const float hi = normed(__uint_as_float(q[e] & 0xFFFF0000u), r,
+                                  __uint_as_float(ww[e] & 0xFFFF0000u));
+          o[e] = float_to_bf16_bits(lo) | (static_cast<uint32_t>(float_to_bf16_bits(hi)) << 16);
+        }
+        stg_stream(orow + c, make_uint4(o[0], o[1], o[2], o[3]));
+      }
+    }
+  }
+  if (threadIdx.x == 0 && *abort_flag) {
+    // a wait ran out: record it, then let the copies this CTA issued land
+    atomicExch(&g_bw_error, 1);
+    for (int j = i; j < i + stages; ++j) {
+      if (blockIdx.x + static_cast<long long>(j) * gridDim.x >= T) break;
+      for (uint32_t n = 0; n < sm100::kSpinLimit && !sm100::mbar_try_wait(&full[j % stages], (j / stages) & 1);
+           ++n) {
+      }
     }
   }
 }
@@ -223,6 +306,40 @@ static int sm_count() {
   return n;
 }
 
+// Ring depth: up to 4 row buffers within 48 KB of shared memory (at least 2).
+template <int NV>
+static cudaError_t launch_rms_ring(void* out, const void* x, const void* w, int hv, long long T,
+                                   double count, float eps, cudaStream_t st) {
+  auto kern = rms_norm_ring_kernel<NV>;
+  const int slot = (hv * 16 + 127) & ~127;
+  int stages = (48 * 1024) / slot;
+  stages = stages < 2 ? 2 : (stages > 4 ? 4 : stages);
+  const int smem = stages * slot + stages * 8 + 2 * (kRmsThreads / 32) * 8 + 16;
+  static int configured = 0;
+  if (smem > 48 * 1024 && configured < smem) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    configured = smem;
+  }
+  int per_sm = 1;
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kRmsThreads, smem);
+  if (per_sm < 1) per_sm = 1;
+  const long long cap = static_cast<long long>(sm_count()) * per_sm;
+  const int grid = static_cast<int>(T < cap ? T : cap);
+  kern<<<grid, kRmsThreads, smem, st>>>(static_cast<const uint8_t*>(x), static_cast<const uint4*>(w),
+                                        static_cast<uint4*>(out), hv, T, stages, count, eps);
+  return cudaGetLastError();
+}
+
+orError_t read_error(int* flag, bool reset) {
+  MCPU_CUDA_TRY(cudaMemcpyFromSymbol(flag, g_bw_error, sizeof(int)), "rms_norm error flag");
+  if (reset) {
+    const int zero = 0;
+    MCPU_CUDA_TRY(cudaMemcpyToSymbol(g_bw_error, &zero, sizeof(int)), "rms_norm error flag reset");
+  }
+  return orSuccess;
+}
+
 }  // namespace bw
 }  // namespace mcpu
 
@@ -239,9 +356,13 @@ extern "C" orError_t mcpu_silu_and_mul(void* out, const void* x, int64_t num_tok
   const bool vec = d % 8 == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0 &&
                    reinterpret_cast<uintptr_t>(out) % 16 == 0;
   const int blocks = bw::sm_count() * 8;
-  if (vec) {
-    bw::silu_and_mul_vec_kernel<<<blocks, 256, 0, st>>>(static_cast<const uint4*>(x),
-                                                         static_cast<uint4*>(out), num_tokens, d / 8);
+  if (vec && d / 8 >= 256 && d / 8 <= 0x7FFFFFFF) {
+    const long long grid = num_tokens < blocks ? num_tokens : blocks;
+    bw::silu_and_mul_rows_kernel<<<static_cast<unsigned>(grid), 256, 0, st>>>(
+        static_cast<const uint4*>(x), static_cast<uint4*>(out), num_tokens, static_cast<int>(d / 8));
+  } else if (vec) {
+    bw::silu_and_mul_flat_kernel<<<blocks, 256, 0, st>>>(static_cast<const uint4*>(x),
+                                                          static_cast<uint4*>(out), num_tokens, d / 8);
   } else {
     bw::silu_and_mul_scalar_kernel<<<blocks, 256, 0, st>>>(static_cast<const uint16_t*>(x),
                                                            static_cast<uint16_t*>(out), num_tokens, d);
@@ -258,15 +379,20 @@ extern "C" orError_t mcpu_rms_norm(void* out, const void* x, const void* weight,
   if (num_tokens == 0) return orSuccess;
   MCPU_ARG_CHECK(out && x && weight, "rms_norm: NULL tensor pointer");
   cudaStream_t st = as_cuda(stream);
-  const bool vec = hidden % 8 == 0 && hidden / 8 <= bw::kRmsThreads * bw::kRmsMaxVec &&
-                   reinterpret_cast<uintptr_t>(x) % 16 == 0 &&
-                   reinterpret_cast<uintptr_t>(out) % 16 == 0 &&
-                   reinterpret_cast<uintptr_t>(weight) % 16 == 0;
+  const int hv = static_cast<int>(hidden / 8);
+  const bool ring = hidden % 8 == 0 && hv <= bw::kRmsThreads * 8 &&
+                    reinterpret_cast<uintptr_t>(x) % 16 == 0 &&
+                    reinterpret_cast<uintptr_t>(out) % 16 == 0 &&
+                    reinterpret_cast<uintptr_t>(weight) % 16 == 0;
   const double count = static_cast<double>(hidden);
-  if (vec) {
-    bw::rms_norm_vec_kernel<<<static_cast<unsigned>(num_tokens), bw::kRmsThreads, 0, st>>>(
-        static_cast<const uint4*>(x), static_cast<const uint4*>(weight), static_cast<uint4*>(out),
-        static_cast<int>(hidden / 8), count, eps);
+  if (ring) {
+    const int nv = (hv + bw::kRmsThreads - 1) / bw::kRmsThreads;
+    cudaError_t e;
+    if (nv <= 1) e = bw::launch_rms_ring<1>(out, x, weight, hv, num_tokens, count, eps, st);
+    else if (nv <= 2) e = bw::launch_rms_ring<2>(out, x, weight, hv, num_tokens, count, eps, st);
+    else if (nv <= 4) e = bw::launch_rms_ring<4>(out, x, weight, hv, num_tokens, count, eps, st);
+    else e = bw::launch_rms_ring<8>(out, x, weight, hv, num_tokens, count, eps, st);
+    return from_cuda(e, "rms_norm launch");
   } else {
     bw::rms_norm_scalar_kernel<<<static_cast<unsigned>(num_tokens), bw::kRmsThreads, 0, st>>>(
         static_cast<const uint16_t*>(x), static_cast<const uint16_t*>(weight),

@@ -27,6 +27,9 @@ orError_t read_error(int* flag, bool reset);
 namespace router {
 orError_t read_error(int* flag, bool reset);
 }
+namespace bw {
+orError_t read_error(int* flag, bool reset);
+}
 
 inline cudaStream_t as_cuda(orStream_t s) {
   return reinterpret_cast<cudaStream_t>(s);

@@ -315,6 +315,7 @@ __global__ void __launch_bounds__(kThreads) grouped_topk_kernel(const Params p) 
 
 #include "grouped_topk_tma.cuh"
 #include "grouped_topk_g8.cuh"
+#include "grouped_topk_sparse.cuh"
 
 
 namespace mcpu {
@@ -382,6 +383,26 @@ static cudaError_t launch_hot_t(const Params& p, const CUtensorMap& tm, int smem
   return cudaGetLastError();
 }
 
+template <int G, int GS_MAX>
+static cudaError_t launch_sparse_t(const Params& p, const CUtensorMap& tm, int smem, cudaStream_t st) {
+  auto kern = grouped_topk_sparse_kernel<G, GS_MAX>;
+  static int configured = 0;
+  if (configured < smem) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    configured = smem;
+  }
+  constexpr int TPT = kSparseThreads / G;
+  const long long tiles = (p.T + TPT - 1) / TPT;
+  int per_sm = 1;
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kSparseThreads, smem);
+  if (per_sm < 1) per_sm = 1;
+  const long long cap = static_cast<long long>(device_sms()) * per_sm;
+  const int grid = static_cast<int>(tiles < cap ? tiles : cap);
+  kern<<<grid, kSparseThreads, smem, st>>>(tm, p, static_cast<int>(tiles));
+  return cudaGetLastError();
+}
+
 // Which (segment width, group-size bound) the hot kernel is built for.
 template <typename InT, bool kFast>
 static bool dispatch_hot(const Params& p, const CUtensorMap& tm, int smem, cudaStream_t st,
@@ -433,6 +454,16 @@ static orError_t launch_hot(Params p, int dtype, bool fast, cudaStream_t st, boo
     return orSuccess;
   cudaError_t err = cudaSuccess;
   bool ok;
+  // fp32 sigmoid + bias with 8 groups: the sparse-key kernel
+  if (fast && p.G == 8 && p.GS % 4 == 0 && p.GS <= 32 && 2 * p.TG >= p.K &&
+      getenv("MCPU_ROUTER_SPARSE_KEYS")) {
+    const SparseLayout SL = sparse_layout(kSparseThreads / 8, p.E);
+    if (p.GS <= 8) err = launch_sparse_t<8, 8>(p, tm, SL.total, st);
+    else if (p.GS <= 16) err = launch_sparse_t<8, 16>(p, tm, SL.total, st);
+    else err = launch_sparse_t<8, 32>(p, tm, SL.total, st);
+    *handled = true;
+    return from_cuda(err, "grouped_topk launch");
+  }
   if (dtype == MCPU_FLOAT32)
     ok = fast ? dispatch_hot<float, true>(p, tm, L.total, st, &err)
               : dispatch_hot<float, false>(p, tm, L.total, st, &err);

@@ -81,12 +81,14 @@ const char* mcpuGetLastErrorString(void) { return g_last_error; }
 
 orError_t mcpu_device_error(int* flag, int reset) {
   MCPU_ARG_CHECK(flag != nullptr, "mcpu_device_error: flag is NULL");
-  int a = 0, b = 0;
+  int a = 0, b = 0, c = 0;
   orError_t e = gemm::read_error(&a, reset != 0);
   if (e != orSuccess) return e;
   e = router::read_error(&b, reset != 0);
   if (e != orSuccess) return e;
-  *flag = a | b;
+  e = bw::read_error(&c, reset != 0);
+  if (e != orSuccess) return e;
+  *flag = a | b | c;
   return orSuccess;
 }
 

@@ -278,6 +278,30 @@ orError_t orMemPoolTrim(size_t keep_bytes) {
   return from_cuda(cudaMemPoolTrimTo(pool, keep_bytes), "orMemPoolTrim");
 }
 
+orError_t mcpu_mem_get_info(int device, size_t* free_bytes, size_t* total_bytes) {
+  MCPU_ARG_CHECK(free_bytes && total_bytes, "mem_get_info: NULL output");
+  int prev = 0;
+  MCPU_CUDA_TRY(cudaGetDevice(&prev), "mem_get_info");
+  if (device >= 0 && device != prev) MCPU_CUDA_TRY(cudaSetDevice(device), "mem_get_info");
+  const cudaError_t e = cudaMemGetInfo(free_bytes, total_bytes);
+  if (device >= 0 && device != prev) cudaSetDevice(prev);
+  return from_cuda(e, "mem_get_info");
+}
+
+orError_t mcpu_mem_pool_reserved(int device, uint64_t* current, uint64_t* peak) {
+  MCPU_ARG_CHECK(current && peak, "mem_pool_reserved: NULL output");
+  int dev = device;
+  if (dev < 0) MCPU_CUDA_TRY(cudaGetDevice(&dev), "mem_pool_reserved");
+  cudaMemPool_t pool;
+  MCPU_CUDA_TRY(cudaDeviceGetDefaultMemPool(&pool, dev), "mem_pool_reserved");
+  unsigned long long c = 0, h = 0;  // the attributes are 64-bit
+  MCPU_CUDA_TRY(cudaMemPoolGetAttribute(pool, cudaMemPoolAttrReservedMemCurrent, &c), "mem_pool_reserved");
+  MCPU_CUDA_TRY(cudaMemPoolGetAttribute(pool, cudaMemPoolAttrReservedMemHigh, &h), "mem_pool_reserved");
+  *current = c;
+  *peak = h;
+  return orSuccess;
+}
+
 orError_t mcpu_copy_strided(const void* src, int src_dtype, void* dst, int dst_dtype, int ndim,
                             const int64_t* sizes, const int64_t* src_strides,
                             const int64_t* dst_strides, orStream_t stream) {

@@ -82,8 +82,19 @@ const at::Tensor& resize_(const at::Tensor& self, c10::IntArrayRef size,
   int64_t numel = 1;
   for (auto s : size) numel *= s;
   const int64_t need = (self.storage_offset() + numel) * static_cast<int64_t>(self.itemsize());
-  if (need > static_cast<int64_t>(self.storage().nbytes()))
-    at::native::resize_bytes_nocuda(self.storage(), c10::SymInt(need));
+  if (need > static_cast<int64_t>(self.storage().nbytes())) {
+    // grow the storage: new block, old bytes copied on the current stream;
+    // the old block goes back to the stream-ordered allocator after the copy
+    c10::StorageImpl* st = self.storage().unsafeGetStorageImpl();
+    TORCH_CHECK(st->resizable(), "mcpu resize_: the tensor's storage is not resizable");
+    c10::DataPtr fresh = allocator()->allocate(static_cast<size_t>(need));
+    const size_t old = st->nbytes();
+    if (old > 0)
+      MCPU_OK(orMemcpyAsync(fresh.get(), st->data(), old, orMemcpyDeviceToDevice, stream_of(self)),
+              "resize_ copy");
+    st->set_data_ptr_noswap(std::move(fresh));
+    st->set_nbytes(static_cast<size_t>(need));
+  }
   self.unsafeGetTensorImpl()->set_sizes_contiguous(size);
   return self;
 }

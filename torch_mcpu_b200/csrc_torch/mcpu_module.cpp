@@ -4,6 +4,7 @@
 #include <torch/csrc/utils/pybind.h>
 #include <torch/extension.h>
 
+#include "mcpu_launch.h"
 #include "mcpu_torch.h"
 
 namespace mcpu_torch {
@@ -49,6 +50,45 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("_reset_peak_memory_stats", [](int d) { reset_peak(static_cast<c10::DeviceIndex>(d)); });
   m.def("_empty_cache", [] {
     TORCH_CHECK(orMemPoolTrim(0) == orSuccess, "empty_cache: ", mcpuGetLastErrorString());
+  });
+  m.def("_get_default_stream", [](int d) {
+    // stream id 0 of every device is its default stream
+    return py::make_tuple(0, d, static_cast<int>(c10::DeviceType::PrivateUse1));
+  });
+  m.def("_mem_get_info", [](int d) {
+    size_t free_b = 0, total_b = 0;
+    TORCH_CHECK(mcpu_mem_get_info(d, &free_b, &total_b) == orSuccess, "mem_get_info: ",
+                mcpuGetLastErrorString());
+    return py::make_tuple(free_b, total_b);
+  });
+  m.def("_mem_pool_reserved", [](int d) {
+    uint64_t cur = 0, peak = 0;
+    TORCH_CHECK(mcpu_mem_pool_reserved(d, &cur, &peak) == orSuccess, "memory_reserved: ",
+                mcpuGetLastErrorString());
+    return py::make_tuple(cur, peak);
+  });
+  // kernel timing of the launch API (include/mcpu_launch.h)
+  m.def("_set_kernel_timing_enabled", [](bool on) { at::mcpu::kernel_timing::set_enabled(on); });
+  m.def("_reset_kernel_timing", [] { at::mcpu::kernel_timing::reset(); });
+  m.def("_get_kernel_timing", [] {
+    py::list out;
+    for (const auto& snap : at::mcpu::kernel_timing::snapshot()) {
+      py::list events;
+      for (const auto& e : snap.events) {
+        py::dict ev;
+        ev["name"] = e.name ? e.name : "";
+        ev["stream"] = e.stream;
+        ev["begin_time"] = e.begin_time;
+        ev["end_time"] = e.end_time;
+        ev["elapsed_time"] = static_cast<double>(static_cast<int64_t>(e.end_time - e.begin_time)) / 1000.0;
+        events.append(ev);
+      }
+      py::dict d;
+      d["role"] = snap.role;
+      d["events"] = events;
+      out.append(d);
+    }
+    return out;
   });
   bind_distributed(m);
 }

@@ -5,8 +5,9 @@
 
 Mirrors what `import torch_mcpu` does in the reference
 (torch_mcpu/__init__.py:32-39): renames PrivateUse1 to "mcpu", registers the
-device module `torch.mcpu` (torch_mcpu/openreg/__init__.py:439-479 subset:
-device/stream/memory/synchronize), generates the tensor methods
+device module `torch.mcpu` (torch_mcpu/openreg/__init__.py:439-479: device,
+streams, memory, kernel timing, synchronize; the op-timing profiler hooks
+and the host-view helpers of the simulated device are not part of it), generates the tensor methods
 (`.mcpu()`, `.is_mcpu`) and registers the "mcpu" distributed backend
 (torch_mcpu/distributed.py:11-20), here backed by NCCL.
 """
@@ -73,8 +74,116 @@ def current_stream_handle(device=None) -> int:
     return _C._current_stream_handle(idx)
 
 
+def _index(device) -> int:
+    if device is None:
+        return current_device()
+    if isinstance(device, int):
+        return device
+    idx = torch.device(device).index
+    return current_device() if idx is None else idx
+
+
+class device:
+    """Context manager that makes `device` current (torch.mcpu.device)."""
+
+    def __init__(self, device):
+        self.idx = -1 if device is None else _index(device)
+        self.prev = -1
+
+    def __enter__(self):
+        self.prev = current_device()
+        if self.idx >= 0 and self.idx != self.prev:
+            _C._set_device(self.idx)
+
+    def __exit__(self, *a):
+        if self.idx >= 0 and self.idx != self.prev:
+            _C._set_device(self.prev)
+        return False
+
+
+class Stream(torch.Stream):
+    """An mcpu stream (a CUDA stream underneath)."""
+
+    def __new__(cls, device=None, priority=0, **kwargs):
+        if kwargs:
+            return super().__new__(cls, priority=priority, **kwargs)
+        return super().__new__(cls, device=torch.device("mcpu", _index(device)), priority=priority)
+
+
+class StreamContext:
+    """Selects a stream for the scope of a `with` block (no-op for None)."""
+
+    def __init__(self, stream):
+        self.stream = stream
+        self.prev = None
+
+    def __enter__(self):
+        if self.stream is not None:
+            self.prev = torch.accelerator.current_stream(self.stream.device)
+            torch.accelerator.set_stream(self.stream)
+        return self.stream
+
+    def __exit__(self, *a):
+        if self.stream is not None:
+            torch.accelerator.set_stream(self.prev)
+        return False
+
+
+def stream(stream) -> StreamContext:
+    return StreamContext(stream)
+
+
+def current_stream(device=None) -> torch.Stream:
+    return torch.accelerator.current_stream(torch.device("mcpu", _index(device)))
+
+
+def default_stream(device=None) -> torch.Stream:
+    sid, idx, dtype = _C._get_default_stream(_index(device))
+    return torch.Stream(stream_id=sid, device_type=dtype, device_index=idx)
+
+
+def set_stream(stream) -> None:
+    if stream is not None:
+        torch.accelerator.set_stream(stream)
+
+
+def set_kernel_timing_enabled(enabled: bool) -> None:
+    _C._set_kernel_timing_enabled(bool(enabled))
+
+
+def reset_kernel_timing() -> None:
+    _C._reset_kernel_timing()
+
+
+def get_kernel_timing() -> list:
+    """[{"role", "events": [{"name", "stream", "begin_time", "end_time",
+    "elapsed_time"(us)}]}] for launches made through the launch API."""
+    return _C._get_kernel_timing()
+
+
+def get_memory_info(device=None) -> tuple:
+    """(free, total) bytes of the device."""
+    return tuple(_C._mem_get_info(_index(device)))
+
+
+mem_get_info = get_memory_info
+
+
 def memory_stats(device=None) -> dict:
-    return dict(_C._memory_stats(current_device() if device is None else int(device)))
+    idx = _index(device)
+    st = dict(_C._memory_stats(idx))
+    cur, peak = _C._mem_pool_reserved(idx)
+    st["reserved_bytes.all.current"] = cur
+    st["reserved_bytes.all.peak"] = peak
+    return st
+
+
+def memory_reserved(device=None) -> int:
+    return memory_stats(device)["reserved_bytes.all.current"]
+
+
+def max_memory_reserved(device=None) -> int:
+    return memory_stats(device)["reserved_bytes.all.peak"]
 
 
 def memory_allocated(device=None) -> int:
@@ -124,8 +233,11 @@ def set_rng_state(state, device=None):
 _module = types.ModuleType("torch.mcpu")
 for _n in ["is_available", "device_count", "current_device", "set_device", "synchronize",
            "current_stream_handle", "memory_stats", "memory_allocated", "max_memory_allocated",
+           "memory_reserved", "max_memory_reserved", "get_memory_info", "mem_get_info",
            "reset_peak_memory_stats", "empty_cache", "is_initialized", "init", "manual_seed",
-           "manual_seed_all", "_is_in_bad_fork", "get_rng_state", "set_rng_state"]:
+           "manual_seed_all", "_is_in_bad_fork", "get_rng_state", "set_rng_state", "device",
+           "Stream", "StreamContext", "stream", "current_stream", "default_stream", "set_stream",
+           "set_kernel_timing_enabled", "reset_kernel_timing", "get_kernel_timing"]:
     setattr(_module, _n, globals()[_n])
 
 
