@@ -56,7 +56,12 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="bound on the host-core baseline's sampling time")
-    return ap.parse_args()
+    ap.add_argument("--legs", default="e2e,bw,mlp,cpu",
+                    help="extra legs besides the router timing (comma list of e2e, bw, mlp, cpu; "
+                         "'none' for the router alone, e.g. under a profiler)")
+    a = ap.parse_args()
+    a.legs = set() if a.legs == "none" else set(a.legs.split(","))
+    return a
 
 
 def workload_config(n):
@@ -287,6 +292,48 @@ def tp_mlp_leg(rank, world, pg, steps, warmup):
     }
 
 
+def bandwidth_leg(dev, reps=20):
+    """silu_and_mul on [8192, 2 x 18432] and rms_norm on [8192, 7168] (bf16,
+    the BASELINE shapes): CUDA-event time per call over rotating inputs
+    larger than L2, achieved GB/s of the algorithmic bytes."""
+    import torch
+
+    from torch_mcpu_b200 import ops
+
+    peak, peak_kind = measured_peaks()
+    out = {}
+    g = torch.Generator(device=dev).manual_seed(7)
+    T1, d = 8192, 18432
+    xs = [torch.randn(T1, 2 * d, generator=g, device=dev).to(torch.bfloat16) for _ in range(2)]
+    o = torch.empty(T1, d, dtype=torch.bfloat16, device=dev)
+    T2, H = 8192, 7168
+    xr = [torch.randn(T2, H, generator=g, device=dev).to(torch.bfloat16) for _ in range(3)]
+    wr = (1 + 0.1 * torch.randn(H, generator=g, device=dev)).to(torch.bfloat16)
+    o2 = torch.empty(T2, H, dtype=torch.bfloat16, device=dev)
+    cases = [
+        ("silu_and_mul", f"x bf16 [{T1}, {2 * d}] -> [{T1}, {d}]", T1 * 2 * d * 2 + T1 * d * 2,
+         lambda i: ops.silu_and_mul(o, xs[i % 2])),
+        ("rms_norm", f"x bf16 [{T2}, {H}], w [{H}], eps 1e-6", 2 * T2 * H * 2 + H * 2,
+         lambda i: ops.rms_norm(o2, xr[i % 3], wr, 1e-6)),
+    ]
+    for name, shape, nbytes, fn in cases:
+        for i in range(3):
+            fn(i)
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(reps):
+            fn(i)
+        e1.record()
+        e1.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / reps
+        gbs = nbytes / (us * 1e-6) / 1e9
+        out[name] = {"shape": shape, "us_per_call": round(us, 2), "algorithmic_bytes": nbytes,
+                     "achieved_gbs": round(gbs, 1), "peak_gbs": peak, "frac": round(gbs / peak, 4),
+                     "peak_kind": peak_kind}
+    return out
+
+
 # ---------------------------------------------------------------- ours
 def run_ours(a):
     import numpy as np
@@ -385,21 +432,24 @@ def run_ours(a):
         _lib.check(lib.orMemcpyAsync(host_w.data_ptr(), w.data_ptr(), T * K * 4, 2, s_handle), "D2H")
         _lib.check(lib.orMemcpyAsync(host_ids.data_ptr(), ids.data_ptr(), T * K * 4, 2, s_handle), "D2H")
 
-    e2e_steps = max(3, min(a.steps, 200))
-    for _ in range(3):
-        e2e_step()
-    stream.synchronize()
-    barrier(pg)
-    with torch.cuda.stream(stream):
-        ev0.record(stream)
-        for _ in range(e2e_steps):
+    e2e_ms = None
+    if "e2e" in a.legs:
+        e2e_steps = max(3, min(a.steps, 200))
+        for _ in range(3):
             e2e_step()
-        ev1.record(stream)
-    ev1.synchronize()
-    barrier(pg)
-    e2e_ms = max_over_ranks(pg, ev0.elapsed_time(ev1)) / e2e_steps
+        stream.synchronize()
+        barrier(pg)
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+            for _ in range(e2e_steps):
+                e2e_step()
+            ev1.record(stream)
+        ev1.synchronize()
+        barrier(pg)
+        e2e_ms = max_over_ranks(pg, ev0.elapsed_time(ev1)) / e2e_steps
     del graph
-    mlp = tp_mlp_leg(rank, world, pg, steps=max(10, min(a.steps, 50)), warmup=3)
+    bw = bandwidth_leg(dev) if "bw" in a.legs else None
+    mlp = tp_mlp_leg(rank, world, pg, steps=max(10, min(a.steps, 50)), warmup=3) if "mlp" in a.legs else None
 
     if rank == 0:
         per_step = ms_max / steps
@@ -430,7 +480,7 @@ def run_ours(a):
                 "traffic": traffic,
                 "algorithmic_bytes_per_launch": BYTES_PER_TOKEN * T,
             },
-            "e2e": {
+            "e2e": None if e2e_ms is None else {
                 "value": round(T * world / (e2e_ms * 1e-3) / 1e6, 2),
                 "unit": "Mtok/s",
                 "h2d_bytes_per_step": h2d,
@@ -440,9 +490,10 @@ def run_ours(a):
             "clocks": clk.summary(),
             "gpu_launches": steps,
             "exact_path_rows_per_step": round(exact_per_step, 2),
+            "bandwidth_ops": bw,
             "tp_mlp": mlp,
         }
-        line["cpu_baseline"] = cpu_baseline(a.cpu_seconds) if world == 1 else None
+        line["cpu_baseline"] = cpu_baseline(a.cpu_seconds) if (world == 1 and "cpu" in a.legs) else None
         print(json.dumps(line), flush=True)
     if pg is not None:
         pg.destroy_process_group()

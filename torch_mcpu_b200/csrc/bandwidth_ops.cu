@@ -42,28 +42,33 @@ __device__ __forceinline__ float rcp_approx(float y) {
 
 __device__ __noinline__ float silu_exact(float a) { return crexp::silu_cr(a); }
 
-// bf16(silu(a)) as the reference computes it.
-__device__ __forceinline__ float silu_bf16(float a) {
+// silu(a) in fp32, good enough to round to the reference's bf16 value: the
+// fast form when its result is clear of a bf16 rounding midpoint, else the
+// reference formula with a correctly rounded exp.
+__device__ __forceinline__ float silu_for_bf16(float a) {
   const float aa = fabsf(a);
   if (aa <= 60.0f) {
     const float e = ex2_approx(__fmul_rn(a, -1.4426950408889634f));
     const float s = __fmul_rn(a, rcp_approx(__fadd_rn(1.0f, e)));
     // error of s against the reference value, in fp32 ulps of s:
     // <= 12 + 2|a|; stay clear of the bf16 midpoint (low half == 0x8000)
-    // with a 2x margin on that bound
+    // with a 2x margin on that bound, 32 + 4 (|a| + 1), bounded from above
+    // with integer work only: at most 36 + (8 << k) for |a| in [2^k, 2^(k+1))
     const int low = static_cast<int>(__float_as_uint(s) & 0xFFFFu) - 0x8000;
-    const int window = 32 + 4 * static_cast<int>(aa + 1.0f);
-    if (abs(low) > window && s != 0.0f) return round_bf16(s);
+    const int ea = static_cast<int>((__float_as_uint(a) >> 23) & 0xFFu) - 127;
+    const int window = 36 + (ea >= 0 ? (8 << ea) : 4);
+    if (abs(low) > window && s != 0.0f) return s;
   }
-  return round_bf16(silu_exact(a));
+  return silu_exact(a);
 }
 
+// out = bf16(bf16(silu(a)) * b) for two bf16 pairs packed in 32-bit words.
 __device__ __forceinline__ uint32_t silu_mul_pair(uint32_t a2, uint32_t b2) {
   const float a0 = __uint_as_float(a2 << 16), a1 = __uint_as_float(a2 & 0xFFFF0000u);
   const float b0 = __uint_as_float(b2 << 16), b1 = __uint_as_float(b2 & 0xFFFF0000u);
-  const uint32_t o0 = float_to_bf16_bits(__fmul_rn(silu_bf16(a0), b0));
-  const uint32_t o1 = float_to_bf16_bits(__fmul_rn(silu_bf16(a1), b1));
-  return o0 | (o1 << 16);
+  const uint32_t s2 = pack_bf16x2(silu_for_bf16(a0), silu_for_bf16(a1));
+  return pack_bf16x2(__fmul_rn(__uint_as_float(s2 << 16), b0),
+                     __fmul_rn(__uint_as_float(s2 & 0xFFFF0000u), b1));
 }
 
 __device__ __forceinline__ uint4 ldg_stream(const uint4* p) {
@@ -146,7 +151,7 @@ __global__ void silu_and_mul_scalar_kernel(const uint16_t* __restrict__ x, uint1
     const long long t = i / d, j = i - t * d;
     const float a = bf16_bits_to_float(x[t * 2 * d + j]);
     const float b = bf16_bits_to_float(x[t * 2 * d + d + j]);
-    out[i] = float_to_bf16_bits(__fmul_rn(silu_bf16(a), b));
+    out[i] = float_to_bf16_bits(__fmul_rn(round_bf16(silu_for_bf16(a)), b));
   }
 }
 
@@ -169,6 +174,11 @@ __device__ __forceinline__ double block_sum(double v, double* smem, bool fail = 
   const int nw = blockDim.x >> 5;
   for (int i = 0; i < nw; ++i) r += smem[i];
   return r;
+}
+
+// x * x of a bf16 value (exact in fp32 for normal products), in double.
+__device__ __forceinline__ double square_as_double(float v) {
+  return static_cast<double>(__fmul_rn(v, v));
 }
 
 __device__ __forceinline__ float normed(float v, float r, float w) {
@@ -222,9 +232,8 @@ __global__ void __launch_bounds__(kRmsThreads, NV <= 4 ? 4 : 1) rms_norm_ring_ke
       const uint32_t q[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const float lo = __uint_as_float(q[e] << 16), hi = __uint_as_float(q[e] & 0xFFFF0000u);
-        acc += static_cast<double>(__fmul_rn(lo, lo));
-        acc += static_cast<double>(__fmul_rn(hi, hi));
+        acc += square_as_double(__uint_as_float(q[e] << 16));
+        acc += square_as_double(__uint_as_float(q[e] & 0xFFFF0000u));
       }
     }
     // after this barrier every thread has read buffer st: refill it (or
@@ -255,10 +264,11 @@ __global__ void __launch_bounds__(kRmsThreads, NV <= 4 ? 4 : 1) rms_norm_ring_ke
         uint32_t o[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float lo = normed(__uint_as_float(q[e] << 16), r, __uint_as_float(ww[e] << 16));
-          const float hi = normed(__uint_as_float(q[e] & 0xFFFF0000u), r,
-                                  __uint_as_float(ww[e] & 0xFFFF0000u));
-          o[e] = float_to_bf16_bits(lo) | (static_cast<uint32_t>(float_to_bf16_bits(hi)) << 16);
+          // y = bf16(x * r) for both halves in one conversion, then bf16(y * w)
+          const uint32_t y2 = pack_bf16x2(__fmul_rn(__uint_as_float(q[e] << 16), r),
+                                          __fmul_rn(__uint_as_float(q[e] & 0xFFFF0000u), r));
+          o[e] = pack_bf16x2(__fmul_rn(__uint_as_float(y2 << 16), __uint_as_float(ww[e] << 16)),
+                             __fmul_rn(__uint_as_float(y2 & 0xFFFF0000u), __uint_as_float(ww[e] & 0xFFFF0000u)));
         }
         stg_stream(orow + c, make_uint4(o[0], o[1], o[2], o[3]));
       }
@@ -286,7 +296,7 @@ __global__ void __launch_bounds__(kRmsThreads) rms_norm_scalar_kernel(
   double acc = 0.0;
   for (long long j = threadIdx.x; j < H; j += blockDim.x) {
     const float v = bf16_bits_to_float(xr[j]);
-    acc += static_cast<double>(__fmul_rn(v, v));
+    acc += square_as_double(v);
   }
   const double total = block_sum(acc, red);
   const float var = static_cast<float>(total / count);

@@ -58,6 +58,13 @@ __device__ __forceinline__ uint16_t float_to_bf16_bits(float f) {
   return __bfloat16_as_ushort(__float2bfloat16_rn(f));
 }
 
+// Two roundings in one conversion instruction: bits of bf16(lo) in the low
+// half, bf16(hi) in the high half.
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
 __device__ __forceinline__ float round_bf16(float f) {
   return bf16_bits_to_float(float_to_bf16_bits(f));
 }

@@ -315,7 +315,7 @@ __global__ void __launch_bounds__(kThreads) grouped_topk_kernel(const Params p) 
 
 #include "grouped_topk_tma.cuh"
 #include "grouped_topk_g8.cuh"
-#include "grouped_topk_sparse.cuh"
+#include "grouped_topk_quad.cuh"
 
 
 namespace mcpu {
@@ -383,23 +383,32 @@ static cudaError_t launch_hot_t(const Params& p, const CUtensorMap& tm, int smem
   return cudaGetLastError();
 }
 
-template <int G, int GS_MAX>
-static cudaError_t launch_sparse_t(const Params& p, const CUtensorMap& tm, int smem, cudaStream_t st) {
-  auto kern = grouped_topk_sparse_kernel<G, GS_MAX>;
+template <int GS_MAX>
+static cudaError_t launch_quad_t(const Params& p, int smem, cudaStream_t st, EncodeTiledFn enc) {
+  auto kern = grouped_topk_quad_kernel<GS_MAX>;
   static int configured = 0;
   if (configured < smem) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     configured = smem;
   }
-  constexpr int TPT = kSparseThreads / G;
-  const long long tiles = (p.T + TPT - 1) / TPT;
+  CUtensorMap tm;
+  cuuint64_t gdim[2] = {static_cast<cuuint64_t>(p.E), static_cast<cuuint64_t>(p.T)};
+  cuuint64_t gstride[1] = {static_cast<cuuint64_t>(p.E) * 4};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(p.E), static_cast<cuuint32_t>(kQuadTokens)};
+  cuuint32_t estr[2] = {1, 1};
+  if (enc(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(p.gating), gdim, gstride, box, estr,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return cudaErrorInvalidValue;
+  const long long wtiles = (p.T + kQuadTokens - 1) / kQuadTokens;
+  const long long ctas_needed = (wtiles + (kQuadThreads / 32) - 1) / (kQuadThreads / 32);
   int per_sm = 1;
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kSparseThreads, smem);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kQuadThreads, smem);
   if (per_sm < 1) per_sm = 1;
   const long long cap = static_cast<long long>(device_sms()) * per_sm;
-  const int grid = static_cast<int>(tiles < cap ? tiles : cap);
-  kern<<<grid, kSparseThreads, smem, st>>>(tm, p, static_cast<int>(tiles));
+  const int grid = static_cast<int>(ctas_needed < cap ? ctas_needed : cap);
+  kern<<<grid, kQuadThreads, smem, st>>>(tm, p, wtiles);
   return cudaGetLastError();
 }
 
@@ -438,6 +447,16 @@ static orError_t launch_hot(Params p, int dtype, bool fast, cudaStream_t st, boo
   static EncodeTiledFn enc = reinterpret_cast<EncodeTiledFn>(driver_entry("cuTensorMapEncodeTiled"));
   if (!enc) return orSuccess;
   if (!(p.G == 8 || (esz == 4 && (p.G == 4 || p.G == 16 || p.G == 32)))) return orSuccess;
+  // fp32 sigmoid + bias with 8 groups: the quad kernel
+  if (fast && p.G == 8 && p.GS % 4 == 0 && p.GS <= 32 && 2 * p.TG >= p.K && (p.T + 7) / 8 <= 0x0FFFFFFF) {
+    cudaError_t err;
+    const QuadLayout QL = quad_layout(p.E);
+    if (p.GS <= 8) err = launch_quad_t<8>(p, QL.total, st, enc);
+    else if (p.GS <= 16) err = launch_quad_t<16>(p, QL.total, st, enc);
+    else err = launch_quad_t<32>(p, QL.total, st, enc);
+    *handled = true;
+    return from_cuda(err, "grouped_topk launch");
+  }
   const int tpt = kHotThreads / p.G;
   const HotLayout L = hot_layout(tpt, p.E, esz);
   if (L.total > 200 * 1024) return orSuccess;
@@ -454,16 +473,6 @@ static orError_t launch_hot(Params p, int dtype, bool fast, cudaStream_t st, boo
     return orSuccess;
   cudaError_t err = cudaSuccess;
   bool ok;
-  // fp32 sigmoid + bias with 8 groups: the sparse-key kernel
-  if (fast && p.G == 8 && p.GS % 4 == 0 && p.GS <= 32 && 2 * p.TG >= p.K &&
-      getenv("MCPU_ROUTER_SPARSE_KEYS")) {
-    const SparseLayout SL = sparse_layout(kSparseThreads / 8, p.E);
-    if (p.GS <= 8) err = launch_sparse_t<8, 8>(p, tm, SL.total, st);
-    else if (p.GS <= 16) err = launch_sparse_t<8, 16>(p, tm, SL.total, st);
-    else err = launch_sparse_t<8, 32>(p, tm, SL.total, st);
-    *handled = true;
-    return from_cuda(err, "grouped_topk launch");
-  }
   if (dtype == MCPU_FLOAT32)
     ok = fast ? dispatch_hot<float, true>(p, tm, L.total, st, &err)
               : dispatch_hot<float, false>(p, tm, L.total, st, &err);
