@@ -146,8 +146,8 @@ OPENREG_EXPORT orError_t mcpu_gemm_swiglu(const void* x, const void* w_gate_up, 
                                           orStream_t stream);
 
 /* *flag = 1 if a kernel on the current device (tensor-core GEMM, TMA-fed
- * router or bulk-copy-fed rms_norm) gave up on a bounded wait since the last
- * reset; that launch left
+ * router or bulk-copy-fed rms_norm) gave up on a bounded wait, or a gather /
+ * scatter met an index out of range, since the last reset; that launch left
  * its output incomplete.  No counterpart in the reference, whose host
  * worker threads report hangs through orStreamSynchronize's timeout. */
 OPENREG_EXPORT orError_t mcpu_device_error(int* flag, int reset);
@@ -195,6 +195,65 @@ OPENREG_EXPORT orError_t mcpu_silu(void* out, const void* x, int64_t n, int dtyp
                                    orStream_t stream);
 OPENREG_EXPORT orError_t mcpu_mul(void* out, const void* a, const void* b, int64_t n, int dtype,
                                   orStream_t stream);
+
+/*
+ * Generic kernels behind the aten registrations the reference's op-by-op
+ * chains use on mcpu tensors (the router function of
+ * tests/test_grouped_topk_compile.py:15-66, vLLM's native silu_and_mul and
+ * rms_norm).  Strided operands of up to 8 dimensions, element strides, 0 for
+ * a broadcast dimension; floating outputs compute in fp32 (fp64 for double),
+ * integer outputs in int64.  Reference: csrc/aten/ops/binary_out.cpp:189-560
+ * and 757-828 (add/sub/mul/div), unary_out.cpp:684-700 (masked_fill_),
+ * reduction_scatter.cpp:116-150, 248-285, 461-495 (max/mean/sum),
+ * topk.cpp:10-40, softmax_random_argmax.cpp:57-82, gather.cpp:10-31.
+ */
+enum { MCPU_BINARY_ADD = 0, MCPU_BINARY_SUB = 1, MCPU_BINARY_MUL = 2, MCPU_BINARY_DIV = 3 };
+enum { MCPU_UNARY_NEG = 0, MCPU_UNARY_RSQRT = 1, MCPU_UNARY_SQRT = 2, MCPU_UNARY_POW_SCALAR = 3,
+       MCPU_UNARY_BITWISE_NOT = 4, MCPU_UNARY_ABS = 5 };
+enum { MCPU_REDUCE_SUM = 0, MCPU_REDUCE_MEAN = 1, MCPU_REDUCE_MAX = 2, MCPU_REDUCE_MIN = 3 };
+
+/* out = a op (alpha * b) for add/sub, a op b otherwise. */
+OPENREG_EXPORT orError_t mcpu_binary(int op, const void* a, int a_dtype, const int64_t* a_strides,
+                                     const void* b, int b_dtype, const int64_t* b_strides, void* out,
+                                     int out_dtype, const int64_t* out_strides, int ndim,
+                                     const int64_t* sizes, double alpha, orStream_t stream);
+/* out = op(x); scalar is the exponent of MCPU_UNARY_POW_SCALAR. */
+OPENREG_EXPORT orError_t mcpu_unary(int op, const void* x, int x_dtype, const int64_t* x_strides,
+                                    void* out, int out_dtype, const int64_t* out_strides, int ndim,
+                                    const int64_t* sizes, double scalar, orStream_t stream);
+/* self[i] = value where mask[i] (mask: bool, broadcast by its strides). */
+OPENREG_EXPORT orError_t mcpu_masked_fill(void* self, int dtype, const int64_t* self_strides,
+                                          const void* mask, const int64_t* mask_strides, int ndim,
+                                          const int64_t* sizes, double fvalue, int64_t ivalue,
+                                          int value_is_float, orStream_t stream);
+/* Reduction of each of `rows` contiguous rows of n elements: sum, mean, or
+ * max / min with the first index of the extreme (NaN propagates); indices
+ * (int64, may be NULL) receive that index. */
+OPENREG_EXPORT orError_t mcpu_reduce_lastdim(int op, const void* x, int dtype, int64_t rows, int64_t n,
+                                             void* out, int out_dtype, int64_t* indices,
+                                             orStream_t stream);
+/* The k largest (largest != 0) or smallest values of each contiguous row,
+ * in order, ties to the lower index, NaN counted as the largest; values
+ * [rows, k] in the input dtype, indices [rows, k] int64. */
+OPENREG_EXPORT orError_t mcpu_topk_lastdim(const void* x, int dtype, int64_t rows, int64_t n, int64_t k,
+                                           int largest, void* values, int64_t* indices,
+                                           orStream_t stream);
+/* Row softmax (or log-softmax) over contiguous rows. */
+OPENREG_EXPORT orError_t mcpu_softmax_lastdim(const void* x, int dtype, int64_t rows, int64_t n,
+                                              void* out, int out_dtype, int log_softmax,
+                                              orStream_t stream);
+/* out[..] = self[.. index[..] ..] along dim; index int64; an index out of
+ * range skips the element and sets the flag mcpu_device_error reports. */
+OPENREG_EXPORT orError_t mcpu_gather(const void* self, int dtype, int ndim, const int64_t* self_sizes,
+                                     const int64_t* self_strides, int64_t dim, const int64_t* index,
+                                     const int64_t* index_sizes, const int64_t* index_strides, void* out,
+                                     const int64_t* out_strides, orStream_t stream);
+/* self[.. index[..] ..] = value along dim (same index rules as gather). */
+OPENREG_EXPORT orError_t mcpu_scatter_value(void* self, int dtype, int ndim, const int64_t* self_sizes,
+                                            const int64_t* self_strides, int64_t dim,
+                                            const int64_t* index, const int64_t* index_sizes,
+                                            const int64_t* index_strides, double fvalue, int64_t ivalue,
+                                            int value_is_float, orStream_t stream);
 
 #ifdef __cplusplus
 }  // extern "C"

@@ -64,6 +64,14 @@ SIGNATURES = {
     "mcpu_device_error": (c_int, [ctypes.POINTER(c_int), c_int]),
     "mcpu_mem_get_info": (c_int, [c_int, ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(ctypes.c_size_t)]),
     "mcpu_mem_pool_reserved": (c_int, [c_int, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64)]),
+    "mcpu_binary": (c_int, [c_int, c_void_p, c_int, ctypes.POINTER(ctypes.c_int64), c_void_p, c_int, ctypes.POINTER(ctypes.c_int64), c_void_p, c_int, ctypes.POINTER(ctypes.c_int64), c_int, ctypes.POINTER(ctypes.c_int64), ctypes.c_double, c_void_p]),
+    "mcpu_unary": (c_int, [c_int, c_void_p, c_int, ctypes.POINTER(ctypes.c_int64), c_void_p, c_int, ctypes.POINTER(ctypes.c_int64), c_int, ctypes.POINTER(ctypes.c_int64), ctypes.c_double, c_void_p]),
+    "mcpu_masked_fill": (c_int, [c_void_p, c_int, ctypes.POINTER(ctypes.c_int64), c_void_p, ctypes.POINTER(ctypes.c_int64), c_int, ctypes.POINTER(ctypes.c_int64), ctypes.c_double, ctypes.c_int64, c_int, c_void_p]),
+    "mcpu_reduce_lastdim": (c_int, [c_int, c_void_p, c_int, ctypes.c_int64, ctypes.c_int64, c_void_p, c_int, c_void_p, c_void_p]),
+    "mcpu_topk_lastdim": (c_int, [c_void_p, c_int, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, c_int, c_void_p, c_void_p, c_void_p]),
+    "mcpu_softmax_lastdim": (c_int, [c_void_p, c_int, ctypes.c_int64, ctypes.c_int64, c_void_p, c_int, c_int, c_void_p]),
+    "mcpu_gather": (c_int, [c_void_p, c_int, c_int, ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64), ctypes.c_int64, c_void_p, ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64), c_void_p, ctypes.POINTER(ctypes.c_int64), c_void_p]),
+    "mcpu_scatter_value": (c_int, [c_void_p, c_int, c_int, ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64), ctypes.c_int64, c_void_p, ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64), ctypes.c_double, ctypes.c_int64, c_int, c_void_p]),
     "mcpu_copy_strided": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p,
                                   c_void_p]),
     "mcpu_fill": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p, ctypes.c_double, c_int64, c_int,

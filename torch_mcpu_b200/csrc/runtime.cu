@@ -88,7 +88,10 @@ orError_t mcpu_device_error(int* flag, int reset) {
   if (e != orSuccess) return e;
   e = bw::read_error(&c, reset != 0);
   if (e != orSuccess) return e;
-  *flag = a | b | c;
+  int d = 0;
+  e = aten_read_error(&d, reset != 0);
+  if (e != orSuccess) return e;
+  *flag = a | b | c | d;
   return orSuccess;
 }
 

@@ -2,7 +2,11 @@
 //
 // The minimal tensor set of the reference (csrc/aten/OpenRegMinimal.cpp:
 // 150-167) plus the hot-path aten ops (mm/addmm: csrc/aten/ops/mm.cpp:115-120;
-// sigmoid/silu: unary_out.cpp:817-836; mul: binary_out.cpp:757-828) and the
+// sigmoid/silu: unary_out.cpp:817-836; add/sub/mul/div: binary_out.cpp:
+// 757-828; sum/mean/max/min: reduction_scatter.cpp:557-578; topk:
+// topk.cpp:43-45; _softmax: softmax_random_argmax.cpp:140-144; gather,
+// scatter, masked_fill, pow, rsqrt, bitwise_not), which let the reference's
+// router function and vLLM's native ops run op by op on mcpu tensors, and the
 // mcpu:: custom ops of the router / MLP path.  Every op enqueues on the
 // current mcpu stream and returns, as the reference's ops do.
 #include <ATen/ATen.h>
@@ -266,23 +270,278 @@ at::Tensor silu(const at::Tensor& self) {
   return silu_out(self, out);
 }
 
-at::Tensor& mul_out(const at::Tensor& self, const at::Tensor& other, at::Tensor& out) {
-  TORCH_CHECK(self.sizes() == other.sizes() && self.scalar_type() == other.scalar_type(),
-              "mul on mcpu (B200): same-shape, same-dtype operands only");
-  TORCH_CHECK(self.scalar_type() == at::kFloat || self.scalar_type() == at::kBFloat16,
-              "mul on mcpu (B200): float32 or bfloat16 only");
-  TORCH_CHECK(out.sizes() == self.sizes() && out.scalar_type() == self.scalar_type(), "mul.out: out must match");
-  const at::Tensor a = self.contiguous(), b = other.contiguous();
-  at::Tensor o = out.is_contiguous() ? out : at::empty(out.sizes(), out.options());
-  MCPU_OK(mcpu_mul(o.data_ptr(), a.const_data_ptr(), b.const_data_ptr(), a.numel(),
-                   dtype_code(a.scalar_type()), stream_of(o)),
-          "mul");
-  if (!o.is_same(out)) strided_copy(o, out);
+// ---------------------------------------------------------------- generic ops
+// Shapes and strides of a tensor as int64 vectors (element strides).
+std::vector<int64_t> vec(c10::IntArrayRef r) { return std::vector<int64_t>(r.begin(), r.end()); }
+
+// A scalar operand (a wrapped number or a 0-dim CPU tensor) as a 0-dim mcpu tensor.
+at::Tensor on_device(const at::Tensor& t, const at::Tensor& like) {
+  if (is_mcpu(t)) return t;
+  TORCH_CHECK(t.dim() == 0, "mcpu: a CPU operand must be a scalar (0-dim), got shape ", t.sizes());
+  at::Tensor d = at::empty({}, like.options().dtype(t.scalar_type()));
+  d.fill_(t.item());
+  return d;
+}
+
+at::Tensor& binary_into(int op, const at::Tensor& self_, const at::Tensor& other_, const at::Scalar& alpha,
+                        at::Tensor& out) {
+  const at::Tensor self = on_device(self_, is_mcpu(self_) ? self_ : other_);
+  const at::Tensor other = on_device(other_, self);
+  const auto shape = at::infer_size(self.sizes(), other.sizes());
+  TORCH_CHECK(out.sizes() == c10::IntArrayRef(shape), "mcpu binary op: out has shape ", out.sizes(),
+              ", expected ", c10::IntArrayRef(shape));
+  const at::Tensor a = self.expand(shape), b = other.expand(shape);
+  const auto sz = vec(out.sizes()), sa = vec(a.strides()), sb = vec(b.strides()), so = vec(out.strides());
+  MCPU_OK(mcpu_binary(op, a.const_data_ptr(), dtype_code(a.scalar_type()), sa.data(), b.const_data_ptr(),
+                      dtype_code(b.scalar_type()), sb.data(), out.data_ptr(), dtype_code(out.scalar_type()),
+                      so.data(), static_cast<int>(out.dim()), sz.data(), alpha.toDouble(), stream_of(out)),
+          "binary op");
   return out;
 }
-at::Tensor mul(const at::Tensor& self, const at::Tensor& other) {
-  at::Tensor out = at::empty(self.sizes(), self.options());
-  return mul_out(self, other, out);
+
+at::ScalarType binary_result(const at::Tensor& a, const at::Tensor& b, bool true_div) {
+  at::ScalarType t = at::result_type(a, b);
+  if (true_div && at::isIntegralType(t, /*includeBool=*/true)) t = c10::typeMetaToScalarType(c10::get_default_dtype());
+  return t;
+}
+
+at::Tensor binary_new(int op, const at::Tensor& self, const at::Tensor& other, const at::Scalar& alpha) {
+  const auto shape = at::infer_size(self.sizes(), other.sizes());
+  const at::Tensor& dev = is_mcpu(self) ? self : other;
+  at::Tensor out = at::empty(shape, dev.options().dtype(binary_result(self, other, op == MCPU_BINARY_DIV)));
+  return binary_into(op, self, other, alpha, out);
+}
+
+at::Tensor add(const at::Tensor& s, const at::Tensor& o, const at::Scalar& alpha) { return binary_new(MCPU_BINARY_ADD, s, o, alpha); }
+at::Tensor& add_out(const at::Tensor& s, const at::Tensor& o, const at::Scalar& alpha, at::Tensor& out) { return binary_into(MCPU_BINARY_ADD, s, o, alpha, out); }
+at::Tensor& add_(at::Tensor& s, const at::Tensor& o, const at::Scalar& alpha) { return binary_into(MCPU_BINARY_ADD, s, o, alpha, s); }
+at::Tensor sub(const at::Tensor& s, const at::Tensor& o, const at::Scalar& alpha) { return binary_new(MCPU_BINARY_SUB, s, o, alpha); }
+at::Tensor& sub_out(const at::Tensor& s, const at::Tensor& o, const at::Scalar& alpha, at::Tensor& out) { return binary_into(MCPU_BINARY_SUB, s, o, alpha, out); }
+at::Tensor mul(const at::Tensor& s, const at::Tensor& o) { return binary_new(MCPU_BINARY_MUL, s, o, 1); }
+at::Tensor& mul_out(const at::Tensor& s, const at::Tensor& o, at::Tensor& out) { return binary_into(MCPU_BINARY_MUL, s, o, 1, out); }
+at::Tensor& mul_(at::Tensor& s, const at::Tensor& o) { return binary_into(MCPU_BINARY_MUL, s, o, 1, s); }
+at::Tensor div_tensor(const at::Tensor& s, const at::Tensor& o) { return binary_new(MCPU_BINARY_DIV, s, o, 1); }
+at::Tensor& div_out(const at::Tensor& s, const at::Tensor& o, at::Tensor& out) { return binary_into(MCPU_BINARY_DIV, s, o, 1, out); }
+at::Tensor& div_(at::Tensor& s, const at::Tensor& o) { return binary_into(MCPU_BINARY_DIV, s, o, 1, s); }
+
+at::Tensor& unary_into(int op, const at::Tensor& self, double scalar, at::Tensor& out) {
+  TORCH_CHECK(out.sizes() == self.sizes(), "mcpu unary op: out must have the input's shape");
+  const auto sz = vec(self.sizes()), sx = vec(self.strides()), so = vec(out.strides());
+  MCPU_OK(mcpu_unary(op, self.const_data_ptr(), dtype_code(self.scalar_type()), sx.data(), out.data_ptr(),
+                     dtype_code(out.scalar_type()), so.data(), static_cast<int>(self.dim()), sz.data(), scalar,
+                     stream_of(out)),
+          "unary op");
+  return out;
+}
+
+at::ScalarType float_result(const at::Tensor& t) {
+  return at::isFloatingType(t.scalar_type()) ? t.scalar_type() : c10::typeMetaToScalarType(c10::get_default_dtype());
+}
+
+at::Tensor neg(const at::Tensor& s) { at::Tensor o = at::empty(s.sizes(), s.options()); return unary_into(MCPU_UNARY_NEG, s, 0, o); }
+at::Tensor& neg_out(const at::Tensor& s, at::Tensor& o) { return unary_into(MCPU_UNARY_NEG, s, 0, o); }
+at::Tensor abs_tensor(const at::Tensor& s) { at::Tensor o = at::empty(s.sizes(), s.options()); return unary_into(MCPU_UNARY_ABS, s, 0, o); }
+at::Tensor& abs_out(const at::Tensor& s, at::Tensor& o) { return unary_into(MCPU_UNARY_ABS, s, 0, o); }
+at::Tensor rsqrt(const at::Tensor& s) { at::Tensor o = at::empty(s.sizes(), s.options().dtype(float_result(s))); return unary_into(MCPU_UNARY_RSQRT, s, 0, o); }
+at::Tensor& rsqrt_out(const at::Tensor& s, at::Tensor& o) { return unary_into(MCPU_UNARY_RSQRT, s, 0, o); }
+at::Tensor sqrt_tensor(const at::Tensor& s) { at::Tensor o = at::empty(s.sizes(), s.options().dtype(float_result(s))); return unary_into(MCPU_UNARY_SQRT, s, 0, o); }
+at::Tensor& sqrt_out(const at::Tensor& s, at::Tensor& o) { return unary_into(MCPU_UNARY_SQRT, s, 0, o); }
+at::Tensor bitwise_not(const at::Tensor& s) {
+  TORCH_CHECK(at::isIntegralType(s.scalar_type(), true), "bitwise_not: integer or bool tensors only");
+  at::Tensor o = at::empty(s.sizes(), s.options());
+  return unary_into(MCPU_UNARY_BITWISE_NOT, s, 0, o);
+}
+at::Tensor& bitwise_not_out(const at::Tensor& s, at::Tensor& o) { return unary_into(MCPU_UNARY_BITWISE_NOT, s, 0, o); }
+at::Tensor pow_scalar(const at::Tensor& s, const at::Scalar& e) {
+  const at::ScalarType t = e.isFloatingPoint() ? float_result(s) : s.scalar_type();
+  at::Tensor o = at::empty(s.sizes(), s.options().dtype(t));
+  return unary_into(MCPU_UNARY_POW_SCALAR, s, e.toDouble(), o);
+}
+at::Tensor& pow_scalar_out(const at::Tensor& s, const at::Scalar& e, at::Tensor& o) {
+  return unary_into(MCPU_UNARY_POW_SCALAR, s, e.toDouble(), o);
+}
+
+at::Tensor& masked_fill_(at::Tensor& self, const at::Tensor& mask_, const at::Scalar& value) {
+  TORCH_CHECK(mask_.scalar_type() == at::kBool, "masked_fill_: the mask must be a bool tensor");
+  const at::Tensor mask = on_device(mask_, self).expand(self.sizes());
+  const auto sz = vec(self.sizes()), ss = vec(self.strides()), sm = vec(mask.strides());
+  MCPU_OK(mcpu_masked_fill(self.data_ptr(), dtype_code(self.scalar_type()), ss.data(), mask.const_data_ptr(),
+                           sm.data(), static_cast<int>(self.dim()), sz.data(), value.toDouble(),
+                           value.isFloatingPoint() ? 0 : value.toLong(), value.isFloatingPoint() ? 1 : 0,
+                           stream_of(self)),
+          "masked_fill_");
+  return self;
+}
+at::Tensor& masked_fill_tensor_(at::Tensor& self, const at::Tensor& mask, const at::Tensor& value) {
+  TORCH_CHECK(value.dim() == 0, "masked_fill_: value must be a 0-dim tensor");
+  return masked_fill_(self, mask, value.item());
+}
+
+// Reductions and selections run over the last dimension of a contiguous
+// tensor; another dimension is moved last first.
+at::Tensor dim_last(const at::Tensor& t, int64_t dim) {
+  return (dim == t.dim() - 1 ? t : t.movedim(dim, -1)).contiguous();
+}
+
+at::Tensor& reduce_into(int op, const at::Tensor& self, int64_t dim, bool keepdim, at::Tensor& values,
+                        at::Tensor* indices) {
+  dim = c10::maybe_wrap_dim(dim, self.dim());
+  const at::Tensor x = dim_last(self, dim);
+  const int64_t n = self.dim() == 0 ? 1 : self.size(dim);
+  const int64_t rows = n == 0 ? x.numel() : x.numel() / n;
+  std::vector<int64_t> shape = vec(self.sizes());
+  if (self.dim() > 0) {
+    if (keepdim) shape[dim] = 1;
+    else shape.erase(shape.begin() + dim);
+  }
+  at::Tensor v = at::empty({rows}, values.options());
+  at::Tensor ix;
+  if (indices) ix = at::empty({rows}, values.options().dtype(at::kLong));
+  MCPU_OK(mcpu_reduce_lastdim(op, x.const_data_ptr(), dtype_code(x.scalar_type()), rows, n, v.data_ptr(),
+                              dtype_code(v.scalar_type()), indices ? ix.data_ptr<int64_t>() : nullptr,
+                              stream_of(x)),
+          "reduction");
+  values.resize_(shape);
+  values.copy_(v.view(shape));
+  if (indices) {
+    indices->resize_(shape);
+    indices->copy_(ix.view(shape));
+  }
+  return values;
+}
+
+at::Tensor sum_dim(const at::Tensor& self, at::OptionalIntArrayRef dims, bool keepdim, std::optional<at::ScalarType> dtype) {
+  at::ScalarType t = dtype.value_or(at::isIntegralType(self.scalar_type(), true) ? at::kLong : self.scalar_type());
+  if (!dims || dims->empty()) {
+    at::Tensor flat = self.reshape({1, self.numel()});
+    at::Tensor out = at::empty({1}, self.options().dtype(t));
+    reduce_into(MCPU_REDUCE_SUM, flat, 1, false, out, nullptr);
+    return keepdim ? out.view(std::vector<int64_t>(self.dim(), 1)) : out.view({});
+  }
+  TORCH_CHECK(dims->size() == 1, "sum on mcpu: one dimension at a time");
+  at::Tensor out = at::empty({0}, self.options().dtype(t));
+  return reduce_into(MCPU_REDUCE_SUM, self, (*dims)[0], keepdim, out, nullptr);
+}
+at::Tensor& sum_dim_out(const at::Tensor& self, at::OptionalIntArrayRef dims, bool keepdim,
+                        std::optional<at::ScalarType> dtype, at::Tensor& out) {
+  TORCH_CHECK(dims && dims->size() == 1, "sum.out on mcpu: one dimension");
+  return reduce_into(MCPU_REDUCE_SUM, self, (*dims)[0], keepdim, out, nullptr);
+}
+at::Tensor mean_dim(const at::Tensor& self, at::OptionalIntArrayRef dims, bool keepdim, std::optional<at::ScalarType> dtype) {
+  TORCH_CHECK(dims && dims->size() == 1, "mean on mcpu: one dimension at a time");
+  at::Tensor out = at::empty({0}, self.options().dtype(dtype.value_or(self.scalar_type())));
+  return reduce_into(MCPU_REDUCE_MEAN, self, (*dims)[0], keepdim, out, nullptr);
+}
+std::tuple<at::Tensor, at::Tensor> max_dim(const at::Tensor& self, int64_t dim, bool keepdim) {
+  at::Tensor v = at::empty({0}, self.options());
+  at::Tensor i = at::empty({0}, self.options().dtype(at::kLong));
+  reduce_into(MCPU_REDUCE_MAX, self, dim, keepdim, v, &i);
+  return {v, i};
+}
+std::tuple<at::Tensor, at::Tensor> min_dim(const at::Tensor& self, int64_t dim, bool keepdim) {
+  at::Tensor v = at::empty({0}, self.options());
+  at::Tensor i = at::empty({0}, self.options().dtype(at::kLong));
+  reduce_into(MCPU_REDUCE_MIN, self, dim, keepdim, v, &i);
+  return {v, i};
+}
+
+std::tuple<at::Tensor&, at::Tensor&> topk_out(const at::Tensor& self, int64_t k, int64_t dim, bool largest,
+                                              bool sorted, at::Tensor& values, at::Tensor& indices) {
+  dim = c10::maybe_wrap_dim(dim, self.dim());
+  const int64_t n = self.dim() == 0 ? 1 : self.size(dim);
+  TORCH_CHECK(k >= 0 && k <= n, "selected index k out of range");
+  const at::Tensor x = dim_last(self, dim);
+  const int64_t rows = n == 0 ? 0 : x.numel() / n;
+  std::vector<int64_t> last_shape = vec(x.sizes());
+  if (!last_shape.empty()) last_shape.back() = k;
+  at::Tensor v = at::empty(last_shape, self.options());
+  at::Tensor ix = at::empty(last_shape, self.options().dtype(at::kLong));
+  MCPU_OK(mcpu_topk_lastdim(x.const_data_ptr(), dtype_code(x.scalar_type()), rows, n, k, largest ? 1 : 0,
+                            v.data_ptr(), ix.data_ptr<int64_t>(), stream_of(x)),
+          "topk");
+  // (sorted or not, the values come in order, ties to the lower index)
+  at::Tensor vv = dim == self.dim() - 1 ? v : v.movedim(-1, dim);
+  at::Tensor ii = dim == self.dim() - 1 ? ix : ix.movedim(-1, dim);
+  values.resize_(vv.sizes());
+  indices.resize_(ii.sizes());
+  values.copy_(vv);
+  indices.copy_(ii);
+  return {values, indices};
+}
+std::tuple<at::Tensor, at::Tensor> topk(const at::Tensor& self, int64_t k, int64_t dim, bool largest, bool sorted) {
+  at::Tensor v = at::empty({0}, self.options());
+  at::Tensor i = at::empty({0}, self.options().dtype(at::kLong));
+  topk_out(self, k, dim, largest, sorted, v, i);
+  return {v, i};
+}
+
+at::Tensor& softmax_into(const at::Tensor& self, int64_t dim, bool log, at::Tensor& out) {
+  dim = c10::maybe_wrap_dim(dim, self.dim());
+  const at::Tensor x = dim_last(self, dim);
+  const int64_t n = self.dim() == 0 ? 1 : self.size(dim);
+  const int64_t rows = n == 0 ? 0 : x.numel() / n;
+  at::Tensor o = at::empty(x.sizes(), out.options());
+  MCPU_OK(mcpu_softmax_lastdim(x.const_data_ptr(), dtype_code(x.scalar_type()), rows, n, o.data_ptr(),
+                               dtype_code(o.scalar_type()), log ? 1 : 0, stream_of(x)),
+          "softmax");
+  at::Tensor oo = dim == self.dim() - 1 ? o : o.movedim(-1, dim);
+  out.resize_(oo.sizes());
+  out.copy_(oo);
+  return out;
+}
+at::Tensor softmax_(const at::Tensor& self, int64_t dim, bool half_to_float) {
+  at::Tensor out = at::empty({0}, self.options().dtype(half_to_float ? at::kFloat : self.scalar_type()));
+  return softmax_into(self, dim, false, out);
+}
+at::Tensor& softmax_out(const at::Tensor& self, int64_t dim, bool half_to_float, at::Tensor& out) {
+  return softmax_into(self, dim, false, out);
+}
+at::Tensor log_softmax_(const at::Tensor& self, int64_t dim, bool half_to_float) {
+  at::Tensor out = at::empty({0}, self.options().dtype(half_to_float ? at::kFloat : self.scalar_type()));
+  return softmax_into(self, dim, true, out);
+}
+
+at::Tensor& gather_out(const at::Tensor& self, int64_t dim, const at::Tensor& index, bool sparse_grad, at::Tensor& out) {
+  dim = c10::maybe_wrap_dim(dim, self.dim());
+  TORCH_CHECK(index.scalar_type() == at::kLong, "gather: index must be int64");
+  TORCH_CHECK(index.dim() == self.dim(), "gather: index and self must have the same number of dimensions");
+  out.resize_(index.sizes());
+  const auto ss = vec(self.sizes()), st = vec(self.strides()), is = vec(index.sizes()), it = vec(index.strides()),
+             ot = vec(out.strides());
+  MCPU_OK(mcpu_gather(self.const_data_ptr(), dtype_code(self.scalar_type()), static_cast<int>(self.dim()), ss.data(),
+                      st.data(), dim, index.const_data_ptr<int64_t>(), is.data(), it.data(), out.data_ptr(), ot.data(),
+                      stream_of(self)),
+          "gather");
+  return out;
+}
+at::Tensor gather(const at::Tensor& self, int64_t dim, const at::Tensor& index, bool sparse_grad) {
+  at::Tensor out = at::empty(index.sizes(), self.options());
+  return gather_out(self, dim, index, sparse_grad, out);
+}
+
+at::Tensor& scatter_value_(at::Tensor& self, int64_t dim, const at::Tensor& index, const at::Scalar& value) {
+  dim = c10::maybe_wrap_dim(dim, self.dim());
+  TORCH_CHECK(index.scalar_type() == at::kLong, "scatter_: index must be int64");
+  TORCH_CHECK(index.dim() == self.dim(), "scatter_: index and self must have the same number of dimensions");
+  const auto ss = vec(self.sizes()), st = vec(self.strides()), is = vec(index.sizes()), it = vec(index.strides());
+  MCPU_OK(mcpu_scatter_value(self.data_ptr(), dtype_code(self.scalar_type()), static_cast<int>(self.dim()), ss.data(),
+                             st.data(), dim, index.const_data_ptr<int64_t>(), is.data(), it.data(), value.toDouble(),
+                             value.isFloatingPoint() ? 0 : value.toLong(), value.isFloatingPoint() ? 1 : 0,
+                             stream_of(self)),
+          "scatter_");
+  return self;
+}
+at::Tensor& scatter_value_out(const at::Tensor& self, int64_t dim, const at::Tensor& index, const at::Scalar& value,
+                              at::Tensor& out) {
+  if (!out.is_same(self)) {
+    out.resize_(self.sizes());
+    out.copy_(self);
+  }
+  return scatter_value_(out, dim, index, value);
+}
+at::Tensor scatter_value(const at::Tensor& self, int64_t dim, const at::Tensor& index, const at::Scalar& value) {
+  at::Tensor out = self.clone();
+  return scatter_value_(out, dim, index, value);
 }
 
 // ---------------------------------------------------------------- custom ops
@@ -369,8 +628,46 @@ TORCH_LIBRARY_IMPL(aten, PrivateUse1, m) {
   m.impl("sigmoid.out", sigmoid_out);
   m.impl("silu", silu);
   m.impl("silu.out", silu_out);
+  m.impl("add.Tensor", add);
+  m.impl("add.out", add_out);
+  m.impl("add_.Tensor", add_);
+  m.impl("sub.Tensor", sub);
+  m.impl("sub.out", sub_out);
   m.impl("mul.Tensor", mul);
   m.impl("mul.out", mul_out);
+  m.impl("mul_.Tensor", mul_);
+  m.impl("div.Tensor", div_tensor);
+  m.impl("div.out", div_out);
+  m.impl("div_.Tensor", div_);
+  m.impl("neg", neg);
+  m.impl("neg.out", neg_out);
+  m.impl("abs", abs_tensor);
+  m.impl("abs.out", abs_out);
+  m.impl("rsqrt", rsqrt);
+  m.impl("rsqrt.out", rsqrt_out);
+  m.impl("sqrt", sqrt_tensor);
+  m.impl("sqrt.out", sqrt_out);
+  m.impl("bitwise_not", bitwise_not);
+  m.impl("bitwise_not.out", bitwise_not_out);
+  m.impl("pow.Tensor_Scalar", pow_scalar);
+  m.impl("pow.Tensor_Scalar_out", pow_scalar_out);
+  m.impl("masked_fill_.Scalar", masked_fill_);
+  m.impl("masked_fill_.Tensor", masked_fill_tensor_);
+  m.impl("sum.dim_IntList", sum_dim);
+  m.impl("sum.IntList_out", sum_dim_out);
+  m.impl("mean.dim", mean_dim);
+  m.impl("max.dim", max_dim);
+  m.impl("min.dim", min_dim);
+  m.impl("topk", topk);
+  m.impl("topk.values", topk_out);
+  m.impl("_softmax", softmax_);
+  m.impl("_softmax.out", softmax_out);
+  m.impl("_log_softmax", log_softmax_);
+  m.impl("gather", gather);
+  m.impl("gather.out", gather_out);
+  m.impl("scatter_.value", scatter_value_);
+  m.impl("scatter.value", scatter_value);
+  m.impl("scatter.value_out", scatter_value_out);
 }
 
 // The reference's TORCH_LIBRARY(mcpu) block (csrc/aten/OpenRegExtra.cpp:
