@@ -163,6 +163,19 @@ OPENREG_EXPORT orError_t mcpu_mem_get_info(int device, size_t* free_bytes, size_
 OPENREG_EXPORT orError_t mcpu_mem_pool_reserved(int device, uint64_t* current, uint64_t* peak);
 
 /*
+ * CUDA graphs of mcpu work (no counterpart in the reference, whose host
+ * queue replays nothing): capture everything enqueued on `stream` (a created
+ * stream, thread-local capture mode) into an executable graph, replay it on
+ * a stream, destroy it.  Work captured must not allocate device memory
+ * (preallocate outputs); a graph holding NCCL calls is destroyed before the
+ * process group is.
+ */
+OPENREG_EXPORT orError_t mcpu_graph_capture_begin(orStream_t stream);
+OPENREG_EXPORT orError_t mcpu_graph_capture_end(orStream_t stream, void** graph_exec);
+OPENREG_EXPORT orError_t mcpu_graph_launch(void* graph_exec, orStream_t stream);
+OPENREG_EXPORT orError_t mcpu_graph_destroy(void* graph_exec);
+
+/*
  * Tensor plumbing of the mcpu device (all asynchronous on `stream`).
  *
  * mcpu_copy_strided: dst[i] = convert(src[i]) over an ndim <= 8 index space

@@ -138,3 +138,25 @@ def test_device_module_api(mcpu):
     del t
     d = torch.mcpu.default_stream()
     assert d.device_type == torch.device("mcpu").type or d.device.type == "mcpu"
+
+
+def test_graph_capture_and_replay(mcpu):
+    g = torch.Generator().manual_seed(5)
+    a = torch.randn(256, 512, generator=g).to(torch.bfloat16).to("mcpu")
+    w = (0.05 * torch.randn(384, 512, generator=g)).to(torch.bfloat16).to("mcpu")
+    out = torch.empty(256, 384, dtype=torch.bfloat16, device="mcpu")
+    side = torch.mcpu.Stream()
+    graph = torch.mcpu.Graph()
+    with torch.mcpu.stream(side):
+        torch.mm(a, w.t(), out=out)  # first call configures the kernel outside the capture
+        side.synchronize()
+        ref = out.cpu().clone()
+        out.zero_()
+        with graph.capture():
+            torch.mm(a, w.t(), out=out)
+        side.synchronize()
+        assert torch.equal(out.cpu(), torch.zeros(256, 384, dtype=torch.bfloat16))  # captured, not run
+        graph.replay()
+        side.synchronize()
+    assert torch.equal(out.cpu(), ref)
+    graph.reset()

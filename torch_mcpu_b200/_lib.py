@@ -64,6 +64,10 @@ SIGNATURES = {
     "mcpu_device_error": (c_int, [ctypes.POINTER(c_int), c_int]),
     "mcpu_mem_get_info": (c_int, [c_int, ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(ctypes.c_size_t)]),
     "mcpu_mem_pool_reserved": (c_int, [c_int, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64)]),
+    "mcpu_graph_capture_begin": (c_int, [c_void_p]),
+    "mcpu_graph_capture_end": (c_int, [c_void_p, ctypes.POINTER(c_void_p)]),
+    "mcpu_graph_launch": (c_int, [c_void_p, c_void_p]),
+    "mcpu_graph_destroy": (c_int, [c_void_p]),
     "mcpu_binary": (c_int, [c_int, c_void_p, c_int, ctypes.POINTER(ctypes.c_int64), c_void_p, c_int, ctypes.POINTER(ctypes.c_int64), c_void_p, c_int, ctypes.POINTER(ctypes.c_int64), c_int, ctypes.POINTER(ctypes.c_int64), ctypes.c_double, c_void_p]),
     "mcpu_unary": (c_int, [c_int, c_void_p, c_int, ctypes.POINTER(ctypes.c_int64), c_void_p, c_int, ctypes.POINTER(ctypes.c_int64), c_int, ctypes.POINTER(ctypes.c_int64), ctypes.c_double, c_void_p]),
     "mcpu_masked_fill": (c_int, [c_void_p, c_int, ctypes.POINTER(ctypes.c_int64), c_void_p, ctypes.POINTER(ctypes.c_int64), c_int, ctypes.POINTER(ctypes.c_int64), ctypes.c_double, ctypes.c_int64, c_int, c_void_p]),

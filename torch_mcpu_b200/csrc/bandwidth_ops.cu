@@ -23,52 +23,46 @@
 
 #include "common.cuh"
 #include "expf_cr.h"
+#include "silu_bf16.cuh"
 #include "sm100.cuh"
 
 namespace mcpu {
 namespace bw {
 
-__device__ __forceinline__ float ex2_approx(float y) {
-  float r;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(y));
-  return r;
-}
 
-__device__ __forceinline__ float rcp_approx(float y) {
-  float r;
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(y));
-  return r;
-}
-
-__device__ __noinline__ float silu_exact(float a) { return crexp::silu_cr(a); }
-
-// silu(a) in fp32, good enough to round to the reference's bf16 value: the
-// fast form when its result is clear of a bf16 rounding midpoint, else the
-// reference formula with a correctly rounded exp.
-__device__ __forceinline__ float silu_for_bf16(float a) {
-  const float aa = fabsf(a);
-  if (aa <= 60.0f) {
-    const float e = ex2_approx(__fmul_rn(a, -1.4426950408889634f));
-    const float s = __fmul_rn(a, rcp_approx(__fadd_rn(1.0f, e)));
-    // error of s against the reference value, in fp32 ulps of s:
-    // <= 12 + 2|a|; stay clear of the bf16 midpoint (low half == 0x8000)
-    // with a 2x margin on that bound, 32 + 4 (|a| + 1), bounded from above
-    // with integer work only: at most 36 + (8 << k) for |a| in [2^k, 2^(k+1))
-    const int low = static_cast<int>(__float_as_uint(s) & 0xFFFFu) - 0x8000;
-    const int ea = static_cast<int>((__float_as_uint(a) >> 23) & 0xFFu) - 127;
-    const int window = 36 + (ea >= 0 ? (8 << ea) : 4);
-    if (abs(low) > window && s != 0.0f) return s;
+// out = bf16(bf16(silu(a)) * b) for 8 bf16 pairs (a and b vectors): the
+// fast silu of all eight, then the few elements whose rounding is not
+// certain redone with the reference formula, then two roundings per
+// conversion instruction.
+__device__ __forceinline__ uint4 silu_mul_vec(uint4 av, uint4 bv) {
+  const uint32_t aw[4] = {av.x, av.y, av.z, av.w};
+  const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
+  float a[8], s[8];
+  uint32_t redo = 0;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    a[2 * q] = __uint_as_float(aw[q] << 16);
+    a[2 * q + 1] = __uint_as_float(aw[q] & 0xFFFF0000u);
   }
-  return silu_exact(a);
-}
-
-// out = bf16(bf16(silu(a)) * b) for two bf16 pairs packed in 32-bit words.
-__device__ __forceinline__ uint32_t silu_mul_pair(uint32_t a2, uint32_t b2) {
-  const float a0 = __uint_as_float(a2 << 16), a1 = __uint_as_float(a2 & 0xFFFF0000u);
-  const float b0 = __uint_as_float(b2 << 16), b1 = __uint_as_float(b2 & 0xFFFF0000u);
-  const uint32_t s2 = pack_bf16x2(silu_for_bf16(a0), silu_for_bf16(a1));
-  return pack_bf16x2(__fmul_rn(__uint_as_float(s2 << 16), b0),
-                     __fmul_rn(__uint_as_float(s2 & 0xFFFF0000u), b1));
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    bool ex;
+    s[j] = silu_fast_checked(a[j], &ex);
+    redo |= ex ? (1u << j) : 0u;
+  }
+  if (redo) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (redo & (1u << j)) s[j] = silu_cr_call(a[j]);
+  }
+  uint32_t o[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint32_t s2 = pack_bf16x2(s[2 * q], s[2 * q + 1]);
+    o[q] = pack_bf16x2(__fmul_rn(__uint_as_float(s2 << 16), __uint_as_float(bw[q] << 16)),
+                       __fmul_rn(__uint_as_float(s2 & 0xFFFF0000u), __uint_as_float(bw[q] & 0xFFFF0000u)));
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
 __device__ __forceinline__ uint4 ldg_stream(const uint4* p) {
@@ -104,23 +98,10 @@ __global__ void __launch_bounds__(256) silu_and_mul_rows_kernel(const uint4* __r
         bv[u] = ldg_stream(b + j + u * 256);
       }
 #pragma unroll
-      for (int u = 0; u < 3; ++u) {
-        uint4 r;
-        r.x = silu_mul_pair(av[u].x, bv[u].x);
-        r.y = silu_mul_pair(av[u].y, bv[u].y);
-        r.z = silu_mul_pair(av[u].z, bv[u].z);
-        r.w = silu_mul_pair(av[u].w, bv[u].w);
-        stg_stream(o + j + u * 256, r);
-      }
+      for (int u = 0; u < 3; ++u) stg_stream(o + j + u * 256, silu_mul_vec(av[u], bv[u]));
     }
     for (; j < dv; j += 256) {
-      const uint4 av = ldg_stream(a + j), bv = ldg_stream(b + j);
-      uint4 r;
-      r.x = silu_mul_pair(av.x, bv.x);
-      r.y = silu_mul_pair(av.y, bv.y);
-      r.z = silu_mul_pair(av.z, bv.z);
-      r.w = silu_mul_pair(av.w, bv.w);
-      stg_stream(o + j, r);
+      stg_stream(o + j, silu_mul_vec(ldg_stream(a + j), ldg_stream(b + j)));
     }
   }
 }
@@ -133,13 +114,7 @@ __global__ void __launch_bounds__(256) silu_and_mul_flat_kernel(const uint4* __r
   for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
     const long long t = i / dv, j = i - t * dv;
-    const uint4 av = ldg_stream(x + t * 2 * dv + j), bv = ldg_stream(x + t * 2 * dv + dv + j);
-    uint4 r;
-    r.x = silu_mul_pair(av.x, bv.x);
-    r.y = silu_mul_pair(av.y, bv.y);
-    r.z = silu_mul_pair(av.z, bv.z);
-    r.w = silu_mul_pair(av.w, bv.w);
-    stg_stream(out + i, r);
+    stg_stream(out + i, silu_mul_vec(ldg_stream(x + t * 2 * dv + j), ldg_stream(x + t * 2 * dv + dv + j)));
   }
 }
 

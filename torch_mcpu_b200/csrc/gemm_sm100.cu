@@ -28,7 +28,7 @@
 
 #include "common.cuh"
 #include "sm100.cuh"
-#include "expf_cr.h"
+#include "silu_bf16.cuh"
 
 namespace mcpu {
 namespace gemm {
@@ -65,29 +65,6 @@ struct Smem {
   uint32_t tmem_base;
   int abort;
 };
-
-__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-  return static_cast<uint32_t>(float_to_bf16_bits(lo)) |
-         (static_cast<uint32_t>(float_to_bf16_bits(hi)) << 16);
-}
-
-__device__ __noinline__ float silu_slow(float a) { return crexp::silu_cr(a); }
-
-// bf16(silu(g)) with the reference's formula g / (1 + exp(-g)) and a
-// correctly rounded exp wherever the fast value is near a bf16 midpoint.
-__device__ __forceinline__ float silu_bf16_exact(float a) {
-  const float aa = fabsf(a);
-  if (aa <= 60.0f) {
-    float e, r;
-    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(__fmul_rn(a, -1.4426950408889634f)));
-    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(__fadd_rn(1.0f, e)));
-    const float s = __fmul_rn(a, r);
-    const int low = static_cast<int>(__float_as_uint(s) & 0xFFFFu) - 0x8000;
-    const int window = 32 + 4 * static_cast<int>(aa + 1.0f);
-    if (abs(low) > window && s != 0.0f) return round_bf16(s);
-  }
-  return round_bf16(silu_slow(a));
-}
 
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -223,14 +200,14 @@ __global__ void __launch_bounds__(THREADS, 1)
             uint32_t o[16];
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
-              float v[2];
-#pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                const float gv = round_bf16(__uint_as_float(g[2 * j + h]));
-                const float uv = round_bf16(__uint_as_float(u[2 * j + h]));
-                v[h] = __fmul_rn(silu_bf16_exact(gv), uv);
-              }
-              o[j] = pack_bf16x2(v[0], v[1]);
+              // gate and up rounded to bf16 (the GEMMs' outputs), then
+              // bf16(bf16(silu(gate)) * up); roundings two at a time
+              const uint32_t g2 = pack_bf16x2(__uint_as_float(g[2 * j]), __uint_as_float(g[2 * j + 1]));
+              const uint32_t u2 = pack_bf16x2(__uint_as_float(u[2 * j]), __uint_as_float(u[2 * j + 1]));
+              const uint32_t s2 = pack_bf16x2(silu_for_bf16(__uint_as_float(g2 << 16)),
+                                              silu_for_bf16(__uint_as_float(g2 & 0xFFFF0000u)));
+              o[j] = pack_bf16x2(__fmul_rn(__uint_as_float(s2 << 16), __uint_as_float(u2 << 16)),
+                                 __fmul_rn(__uint_as_float(s2 & 0xFFFF0000u), __uint_as_float(u2 & 0xFFFF0000u)));
             }
             if (col0 + 32 <= out_cols) {
               uint4* dst = reinterpret_cast<uint4*>(crow + col0);

@@ -79,6 +79,36 @@ extern "C" {
 
 const char* mcpuGetLastErrorString(void) { return g_last_error; }
 
+// ------------------------------------------------------------------ graphs
+orError_t mcpu_graph_capture_begin(orStream_t stream) {
+  MCPU_ARG_CHECK(stream != nullptr, "graph capture: a created stream is needed");
+  return from_cuda(cudaStreamBeginCapture(as_cuda(stream), cudaStreamCaptureModeThreadLocal),
+                   "cudaStreamBeginCapture");
+}
+
+orError_t mcpu_graph_capture_end(orStream_t stream, void** graph_exec) {
+  MCPU_ARG_CHECK(stream != nullptr && graph_exec != nullptr, "graph capture end: NULL argument");
+  cudaGraph_t graph = nullptr;
+  MCPU_CUDA_TRY(cudaStreamEndCapture(as_cuda(stream), &graph), "cudaStreamEndCapture");
+  cudaGraphExec_t exec = nullptr;
+  const cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
+  cudaGraphDestroy(graph);
+  if (e != cudaSuccess) return from_cuda(e, "cudaGraphInstantiate");
+  *graph_exec = exec;
+  return orSuccess;
+}
+
+orError_t mcpu_graph_launch(void* graph_exec, orStream_t stream) {
+  MCPU_ARG_CHECK(graph_exec != nullptr, "graph launch: NULL graph");
+  return from_cuda(cudaGraphLaunch(static_cast<cudaGraphExec_t>(graph_exec), as_cuda(stream)),
+                   "cudaGraphLaunch");
+}
+
+orError_t mcpu_graph_destroy(void* graph_exec) {
+  if (!graph_exec) return orSuccess;
+  return from_cuda(cudaGraphExecDestroy(static_cast<cudaGraphExec_t>(graph_exec)), "cudaGraphExecDestroy");
+}
+
 orError_t mcpu_device_error(int* flag, int reset) {
   MCPU_ARG_CHECK(flag != nullptr, "mcpu_device_error: flag is NULL");
   int a = 0, b = 0, c = 0;

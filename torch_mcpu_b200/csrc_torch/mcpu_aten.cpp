@@ -592,15 +592,24 @@ void rms_norm(at::Tensor& out, const at::Tensor& x, const at::Tensor& weight, do
           "rms_norm");
 }
 
-at::Tensor gemm_swiglu(const at::Tensor& x, const at::Tensor& w_gate_up) {
-  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w_gate_up.scalar_type() == at::kBFloat16,
+at::Tensor& gemm_swiglu_out(const at::Tensor& x, const at::Tensor& w_gate_up, at::Tensor& out) {
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w_gate_up.scalar_type() == at::kBFloat16 &&
+                  out.scalar_type() == at::kBFloat16,
               "gemm_swiglu: bfloat16 tensors expected");
-  const at::Tensor a = x.contiguous(), w = w_gate_up.contiguous();
-  at::Tensor out = at::empty({a.size(0), w.size(0) / 2}, a.options());
-  MCPU_OK(mcpu_gemm_swiglu(a.const_data_ptr(), w.const_data_ptr(), out.data_ptr(), a.size(0), w.size(0) / 2,
-                           a.size(1), MCPU_BFLOAT16, stream_of(a)),
+  TORCH_CHECK(x.is_contiguous() && w_gate_up.is_contiguous() && out.is_contiguous(),
+              "gemm_swiglu.out: contiguous tensors expected");
+  TORCH_CHECK(out.dim() == 2 && out.size(0) == x.size(0) && out.size(1) == w_gate_up.size(0) / 2,
+              "gemm_swiglu.out: out must be [M, I]");
+  MCPU_OK(mcpu_gemm_swiglu(x.const_data_ptr(), w_gate_up.const_data_ptr(), out.data_ptr(), x.size(0),
+                           w_gate_up.size(0) / 2, x.size(1), MCPU_BFLOAT16, stream_of(x)),
           "gemm_swiglu");
   return out;
+}
+
+at::Tensor gemm_swiglu(const at::Tensor& x, const at::Tensor& w_gate_up) {
+  const at::Tensor a = x.contiguous(), w = w_gate_up.contiguous();
+  at::Tensor out = at::empty({a.size(0), w.size(0) / 2}, a.options());
+  return gemm_swiglu_out(a, w, out);
 }
 
 }  // namespace
@@ -679,6 +688,7 @@ TORCH_LIBRARY_FRAGMENT(mcpu, m) {
   m.def("silu_and_mul(Tensor(a!) out, Tensor x) -> ()");
   m.def("rms_norm(Tensor(a!) out, Tensor x, Tensor weight, float eps) -> ()");
   m.def("gemm_swiglu(Tensor x, Tensor w_gate_up_interleaved) -> Tensor");
+  m.def("gemm_swiglu.out(Tensor x, Tensor w_gate_up_interleaved, *, Tensor(a!) out) -> Tensor(a!)");
 }
 
 TORCH_LIBRARY_IMPL(mcpu, PrivateUse1, m) {
@@ -687,4 +697,5 @@ TORCH_LIBRARY_IMPL(mcpu, PrivateUse1, m) {
   m.impl("silu_and_mul", silu_and_mul);
   m.impl("rms_norm", rms_norm);
   m.impl("gemm_swiglu", gemm_swiglu);
+  m.impl("gemm_swiglu.out", gemm_swiglu_out);
 }

@@ -67,6 +67,26 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
                 mcpuGetLastErrorString());
     return py::make_tuple(cur, peak);
   });
+  // CUDA graphs of the work enqueued on the current mcpu stream
+  m.def("_graph_begin", [](int d) {
+    TORCH_CHECK(mcpu_graph_capture_begin(current_stream_handle(static_cast<c10::DeviceIndex>(d))) == orSuccess,
+                "graph capture: ", mcpuGetLastErrorString());
+  });
+  m.def("_graph_end", [](int d) {
+    void* exec = nullptr;
+    TORCH_CHECK(mcpu_graph_capture_end(current_stream_handle(static_cast<c10::DeviceIndex>(d)), &exec) == orSuccess,
+                "graph capture: ", mcpuGetLastErrorString());
+    return reinterpret_cast<uintptr_t>(exec);
+  });
+  m.def("_graph_replay", [](uintptr_t exec, int d) {
+    TORCH_CHECK(mcpu_graph_launch(reinterpret_cast<void*>(exec),
+                                  current_stream_handle(static_cast<c10::DeviceIndex>(d))) == orSuccess,
+                "graph replay: ", mcpuGetLastErrorString());
+  });
+  m.def("_graph_destroy", [](uintptr_t exec) {
+    TORCH_CHECK(mcpu_graph_destroy(reinterpret_cast<void*>(exec)) == orSuccess, "graph destroy: ",
+                mcpuGetLastErrorString());
+  });
   // kernel timing of the launch API (include/mcpu_launch.h)
   m.def("_set_kernel_timing_enabled", [](bool on) { at::mcpu::kernel_timing::set_enabled(on); });
   m.def("_reset_kernel_timing", [] { at::mcpu::kernel_timing::reset(); });

@@ -161,6 +161,54 @@ def get_kernel_timing() -> list:
     return _C._get_kernel_timing()
 
 
+class Graph:
+    """A CUDA graph of the work enqueued on the current mcpu stream.
+
+        g = torch.mcpu.Graph()
+        with torch.mcpu.stream(s), g.capture():   # a non-default stream
+            step()                                 # no device allocation inside
+        g.replay()
+
+    Replays run on the current mcpu stream.  Work inside the capture must
+    not allocate device memory (use preallocated outputs / out= ops); a graph
+    holding collectives is reset before the process group is destroyed."""
+
+    def __init__(self):
+        self._exec = 0
+        self._dev = current_device()
+
+    def capture(self):
+        graph = self
+
+        class _Ctx:
+            def __enter__(self):
+                graph._dev = current_device()
+                _C._graph_begin(graph._dev)
+                return graph
+
+            def __exit__(self, *a):
+                graph._exec = _C._graph_end(graph._dev)
+                return False
+
+        return _Ctx()
+
+    def replay(self):
+        if not self._exec:
+            raise RuntimeError("torch.mcpu.Graph: nothing captured")
+        _C._graph_replay(self._exec, self._dev)
+
+    def reset(self):
+        if self._exec:
+            _C._graph_destroy(self._exec)
+            self._exec = 0
+
+    def __del__(self):
+        try:
+            self.reset()
+        except Exception:
+            pass
+
+
 def get_memory_info(device=None) -> tuple:
     """(free, total) bytes of the device."""
     return tuple(_C._mem_get_info(_index(device)))
@@ -237,7 +285,7 @@ for _n in ["is_available", "device_count", "current_device", "set_device", "sync
            "reset_peak_memory_stats", "empty_cache", "is_initialized", "init", "manual_seed",
            "manual_seed_all", "_is_in_bad_fork", "get_rng_state", "set_rng_state", "device",
            "Stream", "StreamContext", "stream", "current_stream", "default_stream", "set_stream",
-           "set_kernel_timing_enabled", "reset_kernel_timing", "get_kernel_timing"]:
+           "set_kernel_timing_enabled", "reset_kernel_timing", "get_kernel_timing", "Graph"]:
     setattr(_module, _n, globals()[_n])
 
 
