@@ -450,7 +450,7 @@ static orError_t launch_hot(Params p, int dtype, bool fast, cudaStream_t st, boo
   // fp32 sigmoid + bias with 8 groups: the quad kernel
   if (fast && p.G == 8 && p.GS % 4 == 0 && p.GS <= 32 && 2 * p.TG >= p.K && (p.T + 7) / 8 <= 0x0FFFFFFF) {
     cudaError_t err;
-    const QuadLayout QL = quad_layout(p.E);
+    const QuadLayout QL = quad_layout(p.E, p.K);
     if (p.GS <= 8) err = launch_quad_t<8>(p, QL.total, st, enc);
     else if (p.GS <= 16) err = launch_quad_t<16>(p, QL.total, st, enc);
     else err = launch_quad_t<32>(p, QL.total, st, enc);

@@ -8,8 +8,8 @@
 // own tiles [8 tokens, E] through ONE shared-memory buffer filled by TMA:
 // the buffer is needed only until the token's candidates are extracted, so
 // it is handed back to TMA then, and the next tile lands while the warp
-// ranks candidates and writes weights.  One buffer per warp keeps about 20
-// warps resident per SM.  Waits are bounded; warps never wait for one another.
+// ranks candidates and writes weights.  One buffer per warp keeps 20 warps
+// resident per SM (three tiles per warp for 65536 tokens).  Waits are bounded; warps never wait for one another.
 //
 // Per token:
 //   keys    every fast key sigmoid_fast(x) + bias is computed once and written
@@ -40,9 +40,9 @@
 namespace mcpu {
 namespace router {
 
-constexpr int kQuadThreads = 64;     // 2 warps per CTA
-constexpr int kQuadTokens = 8;       // tokens per warp tile
-constexpr int kQuadCandStride = 34;  // kCap + 2: the tokens' lists start in different banks
+constexpr int kQuadThreads = 128;  // 4 warps per CTA (5 CTAs, 20 warps per SM)
+constexpr int kQuadTokens = 8;     // tokens per warp tile
+constexpr int kQuadCandStride = kCap;
 
 struct QuadLayout {
   int tile_bytes;  // one [8, E] fp32 tile
@@ -52,14 +52,14 @@ struct QuadLayout {
   int total;
 };
 
-__host__ __device__ inline QuadLayout quad_layout(int E) {
+__host__ __device__ inline QuadLayout quad_layout(int E, int K) {
   QuadLayout L;
   L.tile_bytes = (kQuadTokens * E * 4 + 127) & ~127;
   int off = L.tile_bytes;
   L.cand_off = off;
   off += kQuadTokens * kQuadCandStride * 8;
   L.sel_off = off;
-  off += kQuadTokens * (kMaxK + 1) * 8;
+  off += kQuadTokens * (K + 1) * 8;
   L.bar_off = off;
   off += 16;
   L.warp_bytes = (off + 127) & ~127;
@@ -184,7 +184,7 @@ __device__ __forceinline__ void quad_rank(const unsigned long long* tc, unsigned
 }
 
 template <int GS_MAX>
-__global__ void __launch_bounds__(kQuadThreads, 9) grouped_topk_quad_kernel(
+__global__ void __launch_bounds__(kQuadThreads, 5) grouped_topk_quad_kernel(
     const __grid_constant__ CUtensorMap tm, const Params p, const long long wtiles) {
   constexpr int VE = 4;
   constexpr int NCH_MAX = GS_MAX / VE;
@@ -193,7 +193,7 @@ __global__ void __launch_bounds__(kQuadThreads, 9) grouped_topk_quad_kernel(
   extern __shared__ uint8_t smem_raw[];
   const uint32_t ra = sm100::smem_u32(smem_raw);
   uint8_t* base = smem_raw + ((128 - (ra & 127)) & 127);
-  const QuadLayout L = quad_layout(p.E);
+  const QuadLayout L = quad_layout(p.E, p.K);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   uint8_t* wb = base + warp * L.warp_bytes;
@@ -371,7 +371,7 @@ __global__ void __launch_bounds__(kQuadThreads, 9) grouped_topk_quad_kernel(
     }
     const int C = __shfl_sync(quadmask, incl, 3, 4);
     unsigned long long* tc = cand + t * kQuadCandStride;
-    unsigned long long* ts = sel + t * (kMaxK + 1);
+    unsigned long long* ts = sel + t * (K + 1);
     const bool whole = C > kCap;
     if (!whole) {
       int pos = incl - cnt;
