@@ -233,33 +233,11 @@ def max_over_ranks(pg, v: float, dev=None) -> float:
 
 
 # ---------------------------------------------------------------- TP MLP
-def tp_mlp_leg(rank, world, pg, steps, warmup):
-    """Gated MLP H=4096, I=14336, T=2048 (bf16), tensor-parallel over the
-    N ranks: fused gate/up GEMM + SwiGLU, down GEMM, SUM all-reduce of the
-    partial outputs through the mcpu ProcessGroup (NCCL).  Whole-job TFLOP/s
-    over the slowest rank's CUDA-event time."""
+def _graph_ms(step, pg, steps, warmup):
+    """Captures `step` once in a CUDA graph on a side stream and returns the
+    slowest rank's mean CUDA-event time of `steps` replays (ms)."""
     import torch
 
-    import configs as C
-
-    cfg = C.MLP_M1
-    x, _, wgu, wd = C.mlp_weights(cfg, world, rank)
-    from torch_mcpu_b200 import ops
-
-    xm = x.to("mcpu")
-    wgu_il = ops.interleave_gate_up(wgu).to("mcpu")
-    wdm = wd.to("mcpu")
-    act = torch.empty(cfg.T, wgu.size(0) // 2, dtype=torch.bfloat16, device="mcpu")
-    y = torch.empty(cfg.T, cfg.H, dtype=torch.bfloat16, device="mcpu")
-
-    def step():
-        torch.ops.mcpu.gemm_swiglu.out(xm, wgu_il, out=act)
-        torch.mm(act, wdm.t(), out=y)
-        if pg is not None:
-            pg.all_reduce(y)
-
-    # the step is captured once in a CUDA graph on a side stream (outputs
-    # preallocated), so replays carry no host dispatch cost
     side = torch.mcpu.Stream()
     graph = torch.mcpu.Graph()
     with torch.mcpu.stream(side):
@@ -283,7 +261,51 @@ def tp_mlp_leg(rank, world, pg, steps, warmup):
         e1.record(side)
         e1.synchronize()
     graph.reset()
-    ms = max_over_ranks(pg, e0.elapsed_time(e1)) / steps
+    return max_over_ranks(pg, e0.elapsed_time(e1)) / steps
+
+
+def tp_mlp_leg(rank, world, pg, steps, warmup):
+    """Gated MLP H=4096, I=14336, T=2048 (bf16), tensor-parallel over the
+    N ranks: fused gate/up GEMM + SwiGLU, then the row-parallel down
+    projection and the SUM all-reduce of the partials — at N > 1 as one
+    kernel over NVLink (mm_allreduce in a symmetric window), with the
+    mm + NCCL all-reduce form timed beside it.  Whole-job TFLOP/s over the
+    slowest rank's CUDA-event time."""
+    import torch
+
+    import configs as C
+
+    cfg = C.MLP_M1
+    x, _, wgu, wd = C.mlp_weights(cfg, world, rank)
+    from torch_mcpu_b200 import ops, symm
+
+    xm = x.to("mcpu")
+    wgu_il = ops.interleave_gate_up(wgu).to("mcpu")
+    wdm = wd.to("mcpu")
+    act = torch.empty(cfg.T, wgu.size(0) // 2, dtype=torch.bfloat16, device="mcpu")
+    y = torch.empty(cfg.T, cfg.H, dtype=torch.bfloat16, device="mcpu")
+
+    def step_nccl():
+        torch.ops.mcpu.gemm_swiglu.out(xm, wgu_il, out=act)
+        torch.mm(act, wdm.t(), out=y)
+        if pg is not None:
+            pg.all_reduce(y)
+
+    nccl_ms = _graph_ms(step_nccl, pg, steps, warmup)
+    ms, mode = nccl_ms, "mm + all_reduce over the mcpu ProcessGroup (NCCL)" if world > 1 else "mm"
+    if world > 1:
+        win = symm.SymmetricWindow(symm.window_bytes(cfg.T, cfg.H, world))
+
+        def step_fused():
+            torch.ops.mcpu.gemm_swiglu.out(xm, wgu_il, out=act)
+            symm.mm_allreduce(act, wdm, win)
+
+        ms = _graph_ms(step_fused, pg, steps, warmup)
+        mode = "down projection + all-reduce fused over NVLink (mm_allreduce, symmetric window)"
+        torch.mcpu.synchronize()
+        if ops.device_error():
+            raise RuntimeError("mm_allreduce: a bounded wait ran out during the TP leg")
+        win.close()
     flops = 2 * cfg.T * cfg.H * cfg.I * 3
     peaks = {}
     try:
@@ -296,8 +318,8 @@ def tp_mlp_leg(rank, world, pg, steps, warmup):
     per_gpu = whole / world
     return {
         "config": f"gated MLP bf16 H={cfg.H} I={cfg.I} T={cfg.T} TP={world} (gate/up column-parallel, "
-                  "down row-parallel, SUM all-reduce over the mcpu ProcessGroup; step replayed from a "
-                  "CUDA graph)",
+                  f"down row-parallel; {mode}; step replayed from a CUDA graph)",
+        "nccl_ms_per_step": round(nccl_ms, 4),
         "tflops": round(whole, 1),
         "per_gpu_tflops": round(per_gpu, 1),
         "ms_per_step": round(ms, 4),

@@ -145,6 +145,72 @@ OPENREG_EXPORT orError_t mcpu_gemm_swiglu(const void* x, const void* w_gate_up, 
                                           int64_t M, int64_t I, int64_t K, int dtype,
                                           orStream_t stream);
 
+/*
+ * Symmetric windows: one device buffer of the same size on every rank of a
+ * tensor-parallel group (one process per GPU of one box), each rank mapping
+ * all of them through CUDA IPC so kernels read and write peers' buffers over
+ * NVLink.  The reference has no counterpart: its ProcessGroup stages tensors
+ * through host memory (torch_mcpu/csrc/Distributed.cpp:281-354).
+ *
+ * symm_alloc: cudaMalloc of `bytes`, zero-filled (synchronously), and its
+ * 64-byte IPC handle.  symm_open: maps another rank's handle into this
+ * process (peer access enabled on first use).  symm_close undoes symm_open,
+ * symm_free undoes symm_alloc.  symm_clear zeroes `bytes` at `ptr` on
+ * `stream` (used to reset a window's counters after a failed call).
+ */
+#define MCPU_SYMM_MAX_RANKS 8
+#define MCPU_SYMM_HANDLE_BYTES 64
+
+typedef struct mcpuSymmWindow {
+  int32_t rank;                         /* this process's rank, 0 <= rank < world */
+  int32_t world;                        /* ranks in the group, 1..MCPU_SYMM_MAX_RANKS */
+  uint64_t bytes;                       /* size of every rank's window */
+  void* base[MCPU_SYMM_MAX_RANKS];      /* window of rank r as mapped in this process */
+} mcpuSymmWindow;
+
+OPENREG_EXPORT orError_t mcpu_symm_alloc(uint64_t bytes, void** ptr, uint8_t* handle);
+OPENREG_EXPORT orError_t mcpu_symm_open(const uint8_t* handle, void** ptr);
+OPENREG_EXPORT orError_t mcpu_symm_close(void* ptr);
+OPENREG_EXPORT orError_t mcpu_symm_free(void* ptr);
+OPENREG_EXPORT orError_t mcpu_symm_clear(void* ptr, uint64_t bytes, orStream_t stream);
+
+/*
+ * mm_allreduce: the row-parallel down projection of the TP MLP and the SUM
+ * all-reduce of its partial outputs in one kernel, i.e.
+ *     out = sum over ranks r of bf16(a_r . b_r^T)     (every rank gets out)
+ * with a [M, K] and b [N, K] this rank's shards (bf16, as for mcpu_mm),
+ * N % 256 == 0, K > 0.  Replaces mm (csrc/aten/ops/mm.cpp:13-51) followed
+ * by McpuBackend::allreduce (torch_mcpu/csrc/Distributed.cpp:403-413), the
+ * pair example/01_mlp_tp4/run.py:106-113 runs per step.
+ *
+ * Each rank's tensor-core epilogue sends every 32-row slice of its bf16
+ * partial straight into the window of the slice's owner rank; the owner
+ * sums the `world` partials in fp32 in rank order, rounds once to bf16 and
+ * writes the result into every rank's window.  All ranks therefore hold the
+ * same bits.  *out receives this rank's result: M x N bf16, row-major,
+ * inside its own window; it stays valid until the next mm_allreduce on the
+ * window.  The window must hold mcpu_mm_allreduce_window_bytes(M, N, world)
+ * bytes; every rank calls with the same M, N, K.
+ *
+ * One cooperative launch per call (all its blocks resident on the GPU);
+ * waits on other ranks give up after 2 s and set mcpu_device_error, after
+ * which the window's counters must be cleared on every rank (symm_clear of
+ * the first mcpu_mm_allreduce_control_bytes bytes) before it is used again.
+ * Calls on one window must be ordered on one stream per rank.
+ */
+OPENREG_EXPORT orError_t mcpu_mm_allreduce(const void* a, const void* b, int64_t M, int64_t N,
+                                           int64_t K, int dtype, const mcpuSymmWindow* window,
+                                           void** out, orStream_t stream);
+
+/* Window size mm_allreduce needs for an M x N output over `world` ranks. */
+OPENREG_EXPORT orError_t mcpu_mm_allreduce_window_bytes(int64_t M, int64_t N, int world,
+                                                        uint64_t* bytes);
+
+/* Leading bytes of a window of `bytes` that hold mm_allreduce's counters
+ * (zero whenever no call is in flight). */
+OPENREG_EXPORT orError_t mcpu_mm_allreduce_control_bytes(uint64_t bytes, int world,
+                                                         uint64_t* control_bytes);
+
 /* *flag = 1 if a kernel on the current device (tensor-core GEMM, TMA-fed
  * router or bulk-copy-fed rms_norm) gave up on a bounded wait, or a gather /
  * scatter met an index out of range, since the last reset; that launch left

@@ -57,12 +57,32 @@ def _worker(rank, world, init_file, q):
         y = torch.mm(act, wdm.t())
         dist.all_reduce(y)
         torch.mcpu.synchronize()
-        q.put((rank, r1, r2, r3, y.cpu().view(torch.int16).numpy()))
+        # the same down projection + all-reduce fused over a symmetric
+        # window, twice in a row (the kernel resets its counters), then a
+        # TP=8-sized shard [2048 x 1792] x [4096 x 1792]^T against NCCL
+        from torch_mcpu_b200 import symm
+
+        win = symm.SymmetricWindow(symm.window_bytes(2048, 4096, world))
+        f1 = symm.mm_allreduce(act, wdm, win).cpu()
+        f2 = symm.mm_allreduce(act, wdm, win).cpu()
+        g = torch.Generator().manual_seed(100 + rank)
+        a = torch.randn(2048, 1792, generator=g).to(torch.bfloat16).to("mcpu")
+        b = (0.02 * torch.randn(4096, 1792, generator=g)).to(torch.bfloat16).to("mcpu")
+        big = symm.mm_allreduce(a, b, win).cpu()
+        big_nccl = torch.mm(a, b.t())
+        dist.all_reduce(big_nccl)
+        big_nccl = big_nccl.cpu()
+        torch.mcpu.synchronize()
+        err = ops.device_error()
+        win.close()
+        fused = (f1.view(torch.int16).numpy(), f2.view(torch.int16).numpy(), big.view(torch.int16).numpy(),
+                 big_nccl.view(torch.int16).numpy(), err)
+        q.put((rank, r1, r2, r3, y.cpu().view(torch.int16).numpy(), fused))
         dist.destroy_process_group()
     except Exception as e:  # pragma: no cover - reported to the parent
         import traceback
 
-        q.put((rank, "error", traceback.format_exc(), None, None))
+        q.put((rank, "error", traceback.format_exc(), None, None, None))
 
 
 def test_process_group_collectives_and_tp_step():
@@ -88,7 +108,7 @@ def test_process_group_collectives_and_tp_step():
         res[rank] = rest
     for p in procs:
         p.join(timeout=120)
-    for rank, (r1, r2, r3, y) in res.items():
+    for rank, (r1, r2, r3, y, _) in res.items():
         assert r1 != "error", r2
         assert r1 == [3.0] * 4
         assert r2 == [1.0] * 3
@@ -101,3 +121,17 @@ def test_process_group_collectives_and_tp_step():
         got = oracle.bf16_bits_to_f32(res[rank][3].view(np.uint16))
         assert np.linalg.norm(got - ref) / np.linalg.norm(ref) < 2e-2
     np.testing.assert_array_equal(res[0][3], res[1][3])
+    # fused down projection + all-reduce: the same bits on every rank, on
+    # repeated calls, and within bf16 rounding of NCCL's sum
+    f = [res[r][4] for r in range(world)]
+    for r in range(world):
+        assert f[r][4] == 0, "device error flag set"
+        np.testing.assert_array_equal(f[r][0], f[0][0])
+        np.testing.assert_array_equal(f[r][1], f[0][0])
+        np.testing.assert_array_equal(f[r][2], f[0][2])
+    got = oracle.bf16_bits_to_f32(f[0][0].view(np.uint16))
+    assert np.linalg.norm(got - ref) / np.linalg.norm(ref) < 2e-2
+    big = oracle.bf16_bits_to_f32(f[0][2].view(np.uint16)).astype(np.float64)
+    nccl = oracle.bf16_bits_to_f32(f[0][3].view(np.uint16)).astype(np.float64)
+    # two bf16 roundings apart at most (NCCL may round after each hop)
+    assert np.all(np.abs(big - nccl) <= 2 ** -7 * np.maximum(np.abs(nccl), np.abs(big)) + 1e-6)

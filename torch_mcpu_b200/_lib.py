@@ -15,6 +15,17 @@ _lib = None
 
 c_int, c_int64, c_float, c_void_p = ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p
 
+SYMM_MAX_RANKS = 8
+SYMM_HANDLE_BYTES = 64
+
+
+class SymmWindow(ctypes.Structure):
+    """mcpuSymmWindow of include/mcpu_ops.h."""
+
+    _fields_ = [("rank", ctypes.c_int32), ("world", ctypes.c_int32), ("bytes", ctypes.c_uint64),
+                ("base", c_void_p * SYMM_MAX_RANKS)]
+
+
 # name -> (restype, argtypes); every entry point declared in include/*.h
 SIGNATURES = {
     # include/openreg.h
@@ -61,6 +72,15 @@ SIGNATURES = {
                            c_void_p]),
     "mcpu_gemm_swiglu": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int,
                                  c_void_p]),
+    "mcpu_symm_alloc": (c_int, [ctypes.c_uint64, ctypes.POINTER(c_void_p), c_void_p]),
+    "mcpu_symm_open": (c_int, [c_void_p, ctypes.POINTER(c_void_p)]),
+    "mcpu_symm_close": (c_int, [c_void_p]),
+    "mcpu_symm_free": (c_int, [c_void_p]),
+    "mcpu_symm_clear": (c_int, [c_void_p, ctypes.c_uint64, c_void_p]),
+    "mcpu_mm_allreduce": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int,
+                                  ctypes.POINTER(SymmWindow), ctypes.POINTER(c_void_p), c_void_p]),
+    "mcpu_mm_allreduce_window_bytes": (c_int, [c_int64, c_int64, c_int, ctypes.POINTER(ctypes.c_uint64)]),
+    "mcpu_mm_allreduce_control_bytes": (c_int, [ctypes.c_uint64, c_int, ctypes.POINTER(ctypes.c_uint64)]),
     "mcpu_device_error": (c_int, [ctypes.POINTER(c_int), c_int]),
     "mcpu_mem_get_info": (c_int, [c_int, ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(ctypes.c_size_t)]),
     "mcpu_mem_pool_reserved": (c_int, [c_int, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64)]),

@@ -21,12 +21,34 @@
 //
 // Every mbarrier wait is bounded; a wait that runs out sets the device error
 // flag, the CTA drains what it issued and returns.
+//
+// The same kernel, instantiated with kAR = true, is the row-parallel down
+// projection of the TP MLP fused with the SUM all-reduce of its partials
+// over NVLink (mcpu_mm_allreduce):
+//   phase A  each epilogue warp converts its 32 accumulator rows to bf16 and
+//            writes them, staged through shared memory as full 128-byte
+//            lines, into the window of the slice's owner rank; then it
+//            bumps the owner's four unit counters (release, system scope);
+//   phase B  four more warps per CTA (warps 6-9), running beside the GEMM
+//            from the start, take this rank's units (8 rows x 256 columns
+//            of a slice) in tile order: wait until all ranks' partials have
+//            arrived, sum them in fp32 in rank order, round once to bf16
+//            and store the rows into every rank's output; at the end, one
+//            fence and one increment of every rank's done counter;
+//   finish   one thread waits for its own done counter to reach the number
+//            of units, so the launch ends only when this rank's output is
+//            complete.
+// Counters are reset by their consumer, so a window is reusable by the next
+// call (and by a replayed CUDA graph) without host work.  The launch is
+// cooperative: every CTA is resident, so no wait depends on an unscheduled
+// block.
 #include <cuda.h>
 #include <math.h>
 
 #include <mutex>
 
 #include "common.cuh"
+#include "peer.cuh"
 #include "sm100.cuh"
 #include "silu_bf16.cuh"
 
@@ -41,11 +63,65 @@ constexpr int B_BYTES = BN * BK * 2;   // 32 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int TMEM_COLS = 512;         // two 128x256 fp32 accumulators
 constexpr int THREADS = 192;
+constexpr int REDUCER_WARPS = 4;                       // kAR: phase-B warps 6..9
+constexpr int THREADS_AR = THREADS + 32 * REDUCER_WARPS;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
 
 enum Epilogue { kPlain = 0, kSwiGLU = 1, kBias = 2 };
 
 __device__ int g_error = 0;
+
+// ---- fused all-reduce (kAR): window layout and work units
+namespace ar {
+constexpr int kSliceRows = 32;                               // one epilogue warp's TMEM lanes
+constexpr int kUnitRows = 8;                                 // rows one phase-B unit reduces
+constexpr int kUnitsPerSlice = kSliceRows / kUnitRows;       // 4
+constexpr long long kRowBytes = BN * 2;                      // 512: one slice row of bf16
+constexpr long long kSliceBytes = kSliceRows * kRowBytes;    // 16 KB
+constexpr long long kUnitBytes = kUnitRows * kRowBytes;      // 4 KB
+constexpr long long kCountersOff = 256;                      // u32 done counter at 0
+constexpr long long kAlign = 4096;
+constexpr int kStagingBytes = 4 * kSliceRows * 128;          // 4 warps x 32 rows x 64 bf16
+
+inline long long align_up(long long v) { return (v + kAlign - 1) / kAlign * kAlign; }
+
+// Leading bytes of a window that hold the done counter and one counter per
+// unit of the largest problem the window can hold; fixed for a window, so a
+// later call with another M finds its counters at zero.
+inline long long control_bytes(unsigned long long bytes, int world) {
+  const long long max_slots =
+      static_cast<long long>(bytes / (static_cast<unsigned long long>(world) * kSliceBytes)) + 1;
+  return align_up(kCountersOff + max_slots * kUnitsPerSlice * 4);
+}
+
+struct Layout {
+  int tiles_m, tiles_n, n_slices, slots;
+  long long recv_off, y_off, total;
+};
+
+// Every rank: [control][recv: world x slots slices][y: M x N bf16].  Slice s
+// (= tile * 4 + warp) belongs to rank s % world at slot s / world; rank q's
+// partial of it lands at recv + (q * slots + slot) * kSliceBytes.
+inline Layout layout(long long M, long long N, int world, unsigned long long bytes) {
+  Layout L;
+  L.tiles_m = static_cast<int>((M + BM - 1) / BM);
+  L.tiles_n = static_cast<int>(N / BN);
+  L.n_slices = L.tiles_m * L.tiles_n * kUnitsPerSlice;
+  L.slots = (L.n_slices + world - 1) / world;
+  L.recv_off = control_bytes(bytes, world);
+  L.y_off = align_up(L.recv_off + static_cast<long long>(world) * L.slots * kSliceBytes);
+  L.total = L.y_off + M * N * 2;
+  return L;
+}
+}  // namespace ar
+
+struct ArParams {
+  uint8_t* base[MCPU_SYMM_MAX_RANKS];  // every rank's window, as mapped here
+  int rank, world;
+  int slots;
+  unsigned int units_total;           // units of the whole problem = done target
+  long long recv_off, y_off;
+};
 
 struct Params {
   int M, N, K;       // N = columns of B (for SwiGLU: 2 x output columns)
@@ -54,6 +130,7 @@ struct Params {
   const void* bias;  // bf16 [N] for kBias
   int epilogue;
   int tiles_m, tiles_n;
+  ArParams ar;       // kAR only
 };
 
 struct Smem {
@@ -66,13 +143,128 @@ struct Smem {
   int abort;
 };
 
-__global__ void __launch_bounds__(THREADS, 1)
+static_assert(sizeof(Smem) <= 256, "barrier block overflows its slot");
+constexpr int SMEM_BYTES_AR = SMEM_BYTES + ar::kStagingBytes;
+
+__device__ __forceinline__ void add_bf16x8(float (&a)[8], const uint4& v) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    a[2 * j] = __fadd_rn(a[2 * j], __uint_as_float(w[j] << 16));
+    a[2 * j + 1] = __fadd_rn(a[2 * j + 1], __uint_as_float(w[j] & 0xFFFF0000u));
+  }
+}
+
+__device__ __forceinline__ uint4 pack_bf16x8(const float (&a)[8]) {
+  return make_uint4(pack_bf16x2(a[0], a[1]), pack_bf16x2(a[2], a[3]), pack_bf16x2(a[4], a[5]),
+                    pack_bf16x2(a[6], a[7]));
+}
+
+// One unit of phase B: rows [row0, row0 + 8) x 256 columns.  Every rank's
+// bf16 partial of those rows is read from this rank's slots (RB rows x WMAX
+// ranks = 16 loads of 16 bytes in flight per lane), summed in fp32 in rank
+// order, rounded once and stored into every rank's output (own copy first).
+template <int WMAX>
+__device__ __forceinline__ void ar_reduce_unit(const Params& p, const uint8_t* src, long long src_stride,
+                                               long long row0, long long col_bytes) {
+  using namespace ar;
+  constexpr int RB = (16 / WMAX) < kUnitRows ? (16 / WMAX) : kUnitRows;
+  const int world = p.ar.world, rank = p.ar.rank;
+  const long long ypitch = static_cast<long long>(p.N) * 2;
+#pragma unroll 1
+  for (int r0 = 0; r0 < kUnitRows; r0 += RB) {
+    uint4 v[RB][WMAX];
+#pragma unroll
+    for (int i = 0; i < RB; ++i) {
+#pragma unroll
+      for (int q = 0; q < WMAX; ++q)
+        if (q < world) v[i][q] = peer::ld_cg_v4(src + q * src_stride + (r0 + i) * kRowBytes);
+    }
+#pragma unroll
+    for (int i = 0; i < RB; ++i) {
+      float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int q = 0; q < WMAX; ++q)
+        if (q < world) add_bf16x8(a, v[i][q]);
+      const uint4 o = pack_bf16x8(a);
+      const long long g = row0 + r0 + i;
+      if (g < p.M) {
+        for (int d = 0; d < world; ++d) {
+          const int dr = rank + d < world ? rank + d : rank + d - world;
+          peer::st_v4(p.ar.base[dr] + p.ar.y_off + col_bytes + g * ypitch, o);
+        }
+      }
+    }
+  }
+}
+
+// Phase B for one reducer warp (rslot of nr per CTA), running from the
+// start of the launch beside the GEMM: takes this rank's units in order,
+// waits until all ranks' partials of each have arrived, reduces and
+// broadcasts it; then one fence and one done increment per rank for all
+// its units.  One thread of the grid then waits until this rank's output
+// is complete.
+__device__ __forceinline__ void ar_reducer(const Params& p, int rslot, int nr, int lane) {
+  using namespace ar;
+  const int world = p.ar.world, rank = p.ar.rank;
+  uint32_t* counters = reinterpret_cast<uint32_t*>(p.ar.base[rank] + kCountersOff);
+  const long long src_stride = static_cast<long long>(p.ar.slots) * kSliceBytes;
+  const int n_slices = p.tiles_m * p.tiles_n * kUnitsPerSlice;
+  const int units = p.ar.slots * kUnitsPerSlice;
+  bool ok = true;
+  uint32_t processed = 0;
+  for (int k = blockIdx.x * nr + rslot; k < units; k += gridDim.x * nr) {
+    const int slot = k / kUnitsPerSlice, sub = k % kUnitsPerSlice;
+    const int sidx = slot * world + rank;
+    if (sidx >= n_slices) break;  // k only grows
+    uint32_t got = 1;
+    if (lane == 0) {
+      got = peer::wait_geq_sys(counters + k, static_cast<uint32_t>(world)) ? 1u : 0u;
+      if (got) peer::st_relaxed_sys(counters + k, 0u);
+    }
+    got = __shfl_sync(0xFFFFFFFFu, got, 0);
+    __syncwarp();  // orders lane 0's acquire before the other lanes' loads
+    if (!got) {
+      ok = false;
+      break;
+    }
+    const int t = sidx / kUnitsPerSlice, ws = sidx % kUnitsPerSlice;
+    const long long row0 = static_cast<long long>(t % p.tiles_m) * BM + ws * kSliceRows + sub * kUnitRows;
+    const long long col_bytes = static_cast<long long>(t / p.tiles_m) * BN * 2 + lane * 16;
+    const uint8_t* src = p.ar.base[rank] + p.ar.recv_off + slot * kSliceBytes + sub * kUnitBytes + lane * 16;
+    if (world <= 2)  // two instances only: more make the kernel spill
+      ar_reduce_unit<2>(p, src, src_stride, row0, col_bytes);
+    else
+      ar_reduce_unit<8>(p, src, src_stride, row0, col_bytes);
+    ++processed;
+  }
+  if (processed) {
+    peer::fence_sys();
+    __syncwarp();
+    if (lane < world) peer::red_add_release_sys(reinterpret_cast<uint32_t*>(p.ar.base[lane]), processed);
+  }
+  if (!ok) {
+    if (lane == 0) atomicOr(&g_error, 2);
+    return;
+  }
+  if (blockIdx.x == 0 && rslot == 0 && lane == 0) {
+    uint32_t* done = reinterpret_cast<uint32_t*>(p.ar.base[rank]);
+    if (peer::wait_geq_sys(done, p.ar.units_total))
+      peer::st_relaxed_sys(done, 0u);
+    else
+      atomicOr(&g_error, 2);
+  }
+}
+
+template <bool kAR>
+__global__ void __launch_bounds__(kAR ? THREADS_AR : THREADS, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     const Params p) {
+                     const __grid_constant__ Params p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* tiles = smem_raw + ((1024 - (raw_addr & 1023)) & 1023);
   Smem* s = reinterpret_cast<Smem*>(tiles + STAGES * STAGE_BYTES);
+  uint8_t* staging = tiles + STAGES * STAGE_BYTES + 256;  // kAR only
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   volatile int* abort = &s->abort;
 
@@ -171,7 +363,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     umma_commit(&s->drain);
     for (uint32_t n = 0; n < kSpinLimit && !mbar_try_wait(&s->drain, 0); ++n) {
     }
-  } else if (warp >= 2) {
+  } else if (warp >= 2 && warp < 6) {
     // ------------------------------------------------ epilogue
     const int slice = warp & 3;  // TMEM lanes [32*slice, 32*slice+32)
     const int row_in_tile = slice * 32 + lane;
@@ -185,6 +377,58 @@ __global__ void __launch_bounds__(THREADS, 1)
       const long long grow = static_cast<long long>(m_blk) * BM + row_in_tile;
       const bool row_ok = grow < p.M;
       const uint32_t tbase = tmem_base + acc * BN + (static_cast<uint32_t>(slice * 32) << 16);
+      if constexpr (kAR) {
+        using namespace ar;
+        // this warp's 32 rows of the tile are slice t*4+slice, owned by rank
+        // (t*4+slice) % world; rows past M are zeros (TMA fill) and are sent
+        // all the same, the owner skips them
+        const int sidx = t * kUnitsPerSlice + slice;
+        const int owner = sidx % p.ar.world, slot = sidx / p.ar.world;
+        uint8_t* dst = p.ar.base[owner] + p.ar.recv_off +
+                       (static_cast<long long>(p.ar.rank) * p.ar.slots + slot) * kSliceBytes;
+        uint8_t* stg = staging + slice * (kSliceRows * 128);
+        (void)row_ok;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 64) {
+          uint32_t r0[32], r1[32];
+          tmem_ld32(tbase + c, r0);
+          tmem_ld32(tbase + c + 32, r1);
+          tmem_ld_wait();
+          // lane = row: 64 bf16 as eight 16-byte vectors, vector index XOR
+          // row so the 8 lanes of a shared-memory phase hit distinct banks
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            *reinterpret_cast<uint4*>(stg + lane * 128 + ((q ^ (lane & 7)) << 4)) =
+                make_uint4(pack_bf16x2(__uint_as_float(r0[8 * q]), __uint_as_float(r0[8 * q + 1])),
+                           pack_bf16x2(__uint_as_float(r0[8 * q + 2]), __uint_as_float(r0[8 * q + 3])),
+                           pack_bf16x2(__uint_as_float(r0[8 * q + 4]), __uint_as_float(r0[8 * q + 5])),
+                           pack_bf16x2(__uint_as_float(r0[8 * q + 6]), __uint_as_float(r0[8 * q + 7])));
+            *reinterpret_cast<uint4*>(stg + lane * 128 + (((q + 4) ^ (lane & 7)) << 4)) =
+                make_uint4(pack_bf16x2(__uint_as_float(r1[8 * q]), __uint_as_float(r1[8 * q + 1])),
+                           pack_bf16x2(__uint_as_float(r1[8 * q + 2]), __uint_as_float(r1[8 * q + 3])),
+                           pack_bf16x2(__uint_as_float(r1[8 * q + 4]), __uint_as_float(r1[8 * q + 5])),
+                           pack_bf16x2(__uint_as_float(r1[8 * q + 6]), __uint_as_float(r1[8 * q + 7])));
+          }
+          __syncwarp();
+          // 8 lanes per row: each store instruction writes four whole
+          // 128-byte lines of the owner's slot
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int row = i * 4 + (lane >> 3), cq = lane & 7;
+            const uint4 v = *reinterpret_cast<const uint4*>(stg + row * 128 + ((cq ^ (row & 7)) << 4));
+            peer::st_v4(dst + row * kRowBytes + (c >> 6) * 128 + cq * 16, v);
+          }
+          __syncwarp();
+        }
+        tc_fence_before();
+        mbar_arrive(&s->tmem_empty[acc]);
+        peer::fence_sys();
+        __syncwarp();
+        if (lane < kUnitsPerSlice)
+          peer::red_add_release_sys(
+              reinterpret_cast<uint32_t*>(p.ar.base[owner] + kCountersOff) + slot * kUnitsPerSlice + lane, 1u);
+        continue;
+      }
       uint16_t* crow = static_cast<uint16_t*>(p.C) + grow * p.ldc;
       if (p.epilogue == kSwiGLU) {
         // columns [0,128) of the tile are gate, [128,256) the matching up
@@ -257,6 +501,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_fence_before();
       mbar_arrive(&s->tmem_empty[acc]);
     }
+  } else if (kAR && warp >= 6) {
+    // ------------------------------------------------ reducers (kAR)
+    ar_reducer(p, warp - 6, REDUCER_WARPS, lane);
   }
 
   if (threadIdx.x == 0 && s->abort) atomicExch(&g_error, 1);
@@ -328,7 +575,7 @@ orError_t launch(const void* A, long long lda, const void* B, long long ldb, voi
   if (e != orSuccess) return e;
   static std::once_flag attr_once;
   std::call_once(attr_once, [] {
-    cudaFuncSetAttribute(gemm_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    cudaFuncSetAttribute(gemm_bf16_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
   });
   Params p;
   p.M = static_cast<int>(M);
@@ -344,8 +591,80 @@ orError_t launch(const void* A, long long lda, const void* B, long long ldb, voi
   int ctas = sm_count();
   if (max_ctas > 0 && max_ctas < ctas) ctas = max_ctas;
   if (tiles < ctas) ctas = tiles;
-  gemm_bf16_kernel<<<ctas, THREADS, SMEM_BYTES, st>>>(ta, tb, p);
+  gemm_bf16_kernel<false><<<ctas, THREADS, SMEM_BYTES, st>>>(ta, tb, p);
   return from_cuda(cudaGetLastError(), "mm launch");
+}
+
+// C = sum over ranks of A_r . B_r^T into every rank's window (kAR).
+orError_t launch_allreduce(const void* A, const void* B, long long M, long long N, long long K,
+                           const mcpuSymmWindow* w, void** out, cudaStream_t st) {
+  MCPU_ARG_CHECK(w != nullptr && out != nullptr, "mm_allreduce: NULL window or output slot");
+  MCPU_ARG_CHECK(w->world >= 1 && w->world <= MCPU_SYMM_MAX_RANKS, "mm_allreduce: world %d outside 1..%d",
+                 w->world, MCPU_SYMM_MAX_RANKS);
+  MCPU_ARG_CHECK(w->rank >= 0 && w->rank < w->world, "mm_allreduce: rank %d outside 0..%d", w->rank,
+                 w->world - 1);
+  for (int r = 0; r < w->world; ++r)
+    MCPU_ARG_CHECK(w->base[r] != nullptr && reinterpret_cast<uintptr_t>(w->base[r]) % 256 == 0,
+                   "mm_allreduce: window of rank %d is NULL or not 256-byte aligned", r);
+  MCPU_ARG_CHECK(M > 0 && N > 0 && K > 0, "mm_allreduce: M, N and K must be positive");
+  MCPU_ARG_CHECK(M < (1LL << 31) && N < (1LL << 31) && K < (1LL << 31), "mm_allreduce: dimension too large");
+  MCPU_ARG_CHECK(N % BN == 0, "mm_allreduce: N (%lld) must be a multiple of %d", N, BN);
+  MCPU_ARG_CHECK(reinterpret_cast<uintptr_t>(A) % 16 == 0 && reinterpret_cast<uintptr_t>(B) % 16 == 0,
+                 "mm_allreduce: operands must be 16-byte aligned");
+  MCPU_ARG_CHECK((K * 2) % 16 == 0, "mm_allreduce: K must be a multiple of 8 (TMA stride rule)");
+  const ar::Layout L = ar::layout(M, N, w->world, w->bytes);
+  MCPU_ARG_CHECK(static_cast<unsigned long long>(L.total) <= w->bytes,
+                 "mm_allreduce: the window holds %llu bytes, an %lld x %lld output over %d ranks needs %lld",
+                 static_cast<unsigned long long>(w->bytes), M, N, w->world, L.total);
+  MCPU_ARG_CHECK(static_cast<long long>(L.n_slices) * ar::kUnitsPerSlice < (1LL << 31),
+                 "mm_allreduce: too many units");
+  CUtensorMap ta, tb;
+  orError_t e = make_map(&ta, A, M, K, K, BM);
+  if (e != orSuccess) return e;
+  e = make_map(&tb, B, N, K, K, BN);
+  if (e != orSuccess) return e;
+  static std::once_flag attr_once;
+  std::call_once(attr_once, [] {
+    cudaFuncSetAttribute(gemm_bf16_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES_AR);
+  });
+  int per_sm = 0;
+  MCPU_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemm_bf16_kernel<true>, THREADS_AR,
+                                                              SMEM_BYTES_AR),
+                "mm_allreduce occupancy");
+  MCPU_ARG_CHECK(per_sm >= 1, "mm_allreduce: the kernel does not fit on an SM");
+  Params p;
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.C = nullptr;
+  p.ldc = N;
+  p.bias = nullptr;
+  p.epilogue = kPlain;
+  p.tiles_m = L.tiles_m;
+  p.tiles_n = L.tiles_n;
+  for (int r = 0; r < MCPU_SYMM_MAX_RANKS; ++r)
+    p.ar.base[r] = r < w->world ? static_cast<uint8_t*>(w->base[r]) : nullptr;
+  p.ar.rank = w->rank;
+  p.ar.world = w->world;
+  p.ar.slots = L.slots;
+  p.ar.units_total = static_cast<unsigned int>(L.n_slices * ar::kUnitsPerSlice);
+  p.ar.recv_off = L.recv_off;
+  p.ar.y_off = L.y_off;
+  // one CTA per SM, all resident (cooperative): phase B of a CTA waits on
+  // phase A of CTAs here and on the other ranks
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(sm_count());
+  cfg.blockDim = dim3(THREADS_AR);
+  cfg.dynamicSmemBytes = SMEM_BYTES_AR;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  MCPU_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemm_bf16_kernel<true>, ta, tb, p), "mm_allreduce launch");
+  *out = static_cast<uint8_t*>(w->base[w->rank]) + L.y_off;
+  return orSuccess;
 }
 
 }  // namespace gemm
@@ -380,6 +699,37 @@ extern "C" orError_t mcpu_gemm_swiglu(const void* x, const void* w_gate_up, void
   MCPU_ARG_CHECK(x && w_gate_up && out, "gemm_swiglu: NULL tensor pointer");
   return gemm::launch(x, K, w_gate_up, K, out, I, M, 2 * I, K, gemm::kSwiGLU, nullptr,
                       as_cuda(stream), 0);
+}
+
+extern "C" orError_t mcpu_mm_allreduce(const void* a, const void* b, int64_t M, int64_t N, int64_t K,
+                                       int dtype, const mcpuSymmWindow* window, void** out,
+                                       orStream_t stream) {
+  MCPU_ARG_CHECK(dtype == MCPU_BFLOAT16, "mm_allreduce: only bfloat16 is supported (dtype code %d)", dtype);
+  MCPU_ARG_CHECK(a && b, "mm_allreduce: NULL tensor pointer");
+  return gemm::launch_allreduce(a, b, M, N, K, window, out, as_cuda(stream));
+}
+
+extern "C" orError_t mcpu_mm_allreduce_window_bytes(int64_t M, int64_t N, int world, uint64_t* bytes) {
+  MCPU_ARG_CHECK(bytes != nullptr, "mm_allreduce_window_bytes: NULL output");
+  MCPU_ARG_CHECK(M > 0 && N > 0 && N % gemm::BN == 0, "mm_allreduce_window_bytes: bad M, N");
+  MCPU_ARG_CHECK(world >= 1 && world <= MCPU_SYMM_MAX_RANKS, "mm_allreduce_window_bytes: bad world");
+  // the control block grows with the window: iterate to a size that holds
+  // the layout computed for itself
+  unsigned long long b = 0;
+  for (int i = 0; i < 64; ++i) {
+    const long long need = gemm::ar::layout(M, N, world, b).total;
+    if (static_cast<unsigned long long>(need) <= b) break;
+    b = static_cast<unsigned long long>(gemm::ar::align_up(need));
+  }
+  *bytes = b;
+  return orSuccess;
+}
+
+extern "C" orError_t mcpu_mm_allreduce_control_bytes(uint64_t bytes, int world, uint64_t* control_bytes) {
+  MCPU_ARG_CHECK(control_bytes != nullptr, "mm_allreduce_control_bytes: NULL output");
+  MCPU_ARG_CHECK(world >= 1 && world <= MCPU_SYMM_MAX_RANKS, "mm_allreduce_control_bytes: bad world");
+  *control_bytes = static_cast<uint64_t>(gemm::ar::control_bytes(bytes, world));
+  return orSuccess;
 }
 
 orError_t gemm::read_error(int* flag, bool reset) {

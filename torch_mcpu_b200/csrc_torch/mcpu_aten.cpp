@@ -612,6 +612,27 @@ at::Tensor gemm_swiglu(const at::Tensor& x, const at::Tensor& w_gate_up) {
   return gemm_swiglu_out(a, w, out);
 }
 
+// Row-parallel down projection + SUM all-reduce of the partials in one kernel
+// (mm, csrc/aten/ops/mm.cpp:13-51, then McpuBackend::allreduce,
+// torch_mcpu/csrc/Distributed.cpp:403-413).  `window` is the address of the
+// mcpuSymmWindow a torch_mcpu_b200.symm.SymmetricWindow holds; the result is
+// a view of this rank's window, valid until the next call on that window.
+at::Tensor mm_allreduce(const at::Tensor& a, const at::Tensor& b, int64_t window) {
+  TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16,
+              "mm_allreduce: bfloat16 tensors expected");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.size(1) == b.size(1),
+              "mm_allreduce: a [M, K] and b [N, K] expected");
+  TORCH_CHECK(a.device() == b.device(), "mm_allreduce: a and b must be on one device");
+  TORCH_CHECK(window != 0, "mm_allreduce: NULL window");
+  const at::Tensor ac = a.contiguous(), bc = b.contiguous();
+  void* out = nullptr;
+  MCPU_OK(mcpu_mm_allreduce(ac.const_data_ptr(), bc.const_data_ptr(), ac.size(0), bc.size(0), ac.size(1),
+                            MCPU_BFLOAT16, reinterpret_cast<const mcpuSymmWindow*>(window), &out,
+                            stream_of(ac)),
+          "mm_allreduce");
+  return at::from_blob(out, {ac.size(0), bc.size(0)}, [](void*) {}, ac.options());
+}
+
 }  // namespace
 }  // namespace mcpu_torch
 
@@ -689,6 +710,7 @@ TORCH_LIBRARY_FRAGMENT(mcpu, m) {
   m.def("rms_norm(Tensor(a!) out, Tensor x, Tensor weight, float eps) -> ()");
   m.def("gemm_swiglu(Tensor x, Tensor w_gate_up_interleaved) -> Tensor");
   m.def("gemm_swiglu.out(Tensor x, Tensor w_gate_up_interleaved, *, Tensor(a!) out) -> Tensor(a!)");
+  m.def("mm_allreduce(Tensor a, Tensor b, int window) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(mcpu, PrivateUse1, m) {
@@ -698,4 +720,5 @@ TORCH_LIBRARY_IMPL(mcpu, PrivateUse1, m) {
   m.impl("rms_norm", rms_norm);
   m.impl("gemm_swiglu", gemm_swiglu);
   m.impl("gemm_swiglu.out", gemm_swiglu_out);
+  m.impl("mm_allreduce", mm_allreduce);
 }

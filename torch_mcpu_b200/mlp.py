@@ -10,6 +10,10 @@ configurations, optionally preceded by rms_norm:
     a = silu(h Wg_r^T) * (h Wu_r^T)       one tcgen05 GEMM with fused epilogue
     y_r = a Wd_r^T                        tcgen05 GEMM
     y = all_reduce(sum_r y_r)             NCCL over NVLink (torch.distributed)
+
+or, on mcpu tensors with a symmetric window (mcpu_tp_step), the last two
+lines as one kernel that sends the partial tiles over NVLink as they leave
+the tensor cores (torch_mcpu_b200.symm.mm_allreduce).
 """
 
 from __future__ import annotations
@@ -71,3 +75,24 @@ def run_one_step(model: TPShardSwiGLU, x: torch.Tensor, group=None, out=None) ->
         if torch.distributed.get_world_size(group) > 1:
             torch.distributed.all_reduce(y, group=group)
     return y
+
+
+def mcpu_tp_step(x: torch.Tensor, w_gate_up_interleaved: torch.Tensor, w_down: torch.Tensor,
+                 act: torch.Tensor, window=None, out: torch.Tensor | None = None, group=None) -> torch.Tensor:
+    """One TP MLP step on mcpu tensors (example/01_mlp_tp4/run.py:106-113):
+    fused gate/up GEMM + SwiGLU into `act` [T, I_r], then the row-parallel
+    down projection and the SUM all-reduce, either fused over the symmetric
+    `window` (the result is a view of the window) or as mm into `out` plus
+    an all_reduce through the mcpu ProcessGroup (NCCL)."""
+    torch.ops.mcpu.gemm_swiglu.out(x, w_gate_up_interleaved, out=act)
+    if window is not None:
+        from .symm import mm_allreduce
+
+        return mm_allreduce(act, w_down, window)
+    if out is None:
+        out = torch.empty(x.shape[0], w_down.shape[0], dtype=torch.bfloat16, device=x.device)
+    torch.mm(act, w_down.t(), out=out)
+    if torch.distributed.is_available() and torch.distributed.is_initialized():
+        if torch.distributed.get_world_size(group) > 1:
+            torch.distributed.all_reduce(out, group=group)
+    return out
