@@ -316,7 +316,6 @@ __global__ void __launch_bounds__(kThreads) grouped_topk_kernel(const Params p) 
 #include "grouped_topk_tma.cuh"
 #include "grouped_topk_g8.cuh"
 #include "grouped_topk_quad.cuh"
-#include "grouped_topk_coarse.cuh"
 
 
 namespace mcpu {
@@ -413,35 +412,6 @@ static cudaError_t launch_quad_t(const Params& p, int smem, cudaStream_t st, Enc
   return cudaGetLastError();
 }
 
-template <int GS_MAX>
-static cudaError_t launch_coarse_t(const Params& p, int smem, cudaStream_t st, EncodeTiledFn enc) {
-  auto kern = grouped_topk_coarse_kernel<GS_MAX>;
-  static int configured = 0;
-  if (configured < smem) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return e;
-    configured = smem;
-  }
-  CUtensorMap tm;
-  cuuint64_t gdim[2] = {static_cast<cuuint64_t>(p.E), static_cast<cuuint64_t>(p.T)};
-  cuuint64_t gstride[1] = {static_cast<cuuint64_t>(p.E) * 4};
-  cuuint32_t box[2] = {static_cast<cuuint32_t>(p.E), static_cast<cuuint32_t>(kQuadTokens)};
-  cuuint32_t estr[2] = {1, 1};
-  if (enc(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(p.gating), gdim, gstride, box, estr,
-          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-    return cudaErrorInvalidValue;
-  const long long wtiles = (p.T + kQuadTokens - 1) / kQuadTokens;
-  const long long ctas_needed = (wtiles + (kCoarseThreads / 32) - 1) / (kCoarseThreads / 32);
-  int per_sm = 1;
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kCoarseThreads, smem);
-  if (per_sm < 1) per_sm = 1;
-  const long long cap = static_cast<long long>(device_sms()) * per_sm;
-  const int grid = static_cast<int>(ctas_needed < cap ? ctas_needed : cap);
-  kern<<<grid, kCoarseThreads, smem, st>>>(tm, p, wtiles);
-  return cudaGetLastError();
-}
-
 // Which (segment width, group-size bound) the hot kernel is built for.
 template <typename InT, bool kFast>
 static bool dispatch_hot(const Params& p, const CUtensorMap& tm, int smem, cudaStream_t st,
@@ -477,16 +447,7 @@ static orError_t launch_hot(Params p, int dtype, bool fast, cudaStream_t st, boo
   static EncodeTiledFn enc = reinterpret_cast<EncodeTiledFn>(driver_entry("cuTensorMapEncodeTiled"));
   if (!enc) return orSuccess;
   if (!(p.G == 8 || (esz == 4 && (p.G == 4 || p.G == 16 || p.G == 32)))) return orSuccess;
-  // fp32 sigmoid + bias with 8 groups of 16, 24 or 32: the coarse-key kernel
-  if (fast && p.G == 8 && p.GS % 8 == 0 && p.GS >= 16 && p.GS <= 32 && 2 * p.TG >= p.K &&
-      (p.T + 7) / 8 <= 0x0FFFFFFF) {
-    const CoarseLayout CL = coarse_layout(p.E, p.K);
-    const cudaError_t err = p.GS <= 16 ? launch_coarse_t<16>(p, CL.total, st, enc)
-                                       : launch_coarse_t<32>(p, CL.total, st, enc);
-    *handled = true;
-    return from_cuda(err, "grouped_topk launch");
-  }
-  // other group sizes: the quad kernel
+  // fp32 sigmoid + bias with 8 groups: the quad kernel
   if (fast && p.G == 8 && p.GS % 4 == 0 && p.GS <= 32 && 2 * p.TG >= p.K && (p.T + 7) / 8 <= 0x0FFFFFFF) {
     cudaError_t err;
     const QuadLayout QL = quad_layout(p.E, p.K);
