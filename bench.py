@@ -56,8 +56,8 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="bound on the host-core baseline's sampling time")
-    ap.add_argument("--legs", default="e2e,bw,mlp,cpu",
-                    help="extra legs besides the router timing (comma list of e2e, bw, mlp, cpu; "
+    ap.add_argument("--legs", default="e2e,bw,moe,mlp,cpu",
+                    help="extra legs besides the router timing (comma list of e2e, bw, moe, mlp, cpu; "
                          "'none' for the router alone, e.g. under a profiler)")
     a = ap.parse_args()
     a.legs = set() if a.legs == "none" else set(a.legs.split(","))
@@ -372,6 +372,59 @@ def bandwidth_leg(dev, reps=20):
     return out
 
 
+def moe_leg(dev, ids, stream, reps=8, per_graph=32):
+    """MoE dispatch after the router: moe_align_block_size on the router's
+    own topk_ids [65536, 8] (256 experts, block 64), replayed from a CUDA
+    graph; time per call and GB/s of its algorithmic bytes (ids read once,
+    sorted ids and block experts written once)."""
+    import ctypes
+
+    import torch
+
+    from torch_mcpu_b200 import _lib
+
+    lib = _lib.load()
+    peak, peak_kind = measured_peaks()
+    numel, E_, bs = ids.numel(), 256, 64
+    cap = min(numel + E_ * (bs - 1), numel * bs)
+    nblk = -(-cap // bs)
+    srt = torch.empty(cap, dtype=torch.int32, device=dev)
+    eid = torch.empty(nblk, dtype=torch.int32, device=dev)
+    npad = torch.empty(1, dtype=torch.int32, device=dev)
+    wsb = ctypes.c_uint64()
+    _lib.check(lib.mcpu_moe_align_workspace_bytes(numel, E_, ctypes.byref(wsb)), "moe workspace")
+    work = torch.empty(wsb.value, dtype=torch.uint8, device=dev)
+
+    def call():
+        _lib.check(lib.mcpu_moe_align_block_size(ids.data_ptr(), numel, E_, bs, srt.data_ptr(), cap, eid.data_ptr(),
+                                                 nblk, npad.data_ptr(), work.data_ptr(), wsb.value,
+                                                 stream.cuda_stream), "moe_align_block_size")
+
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            call()
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for _ in range(per_graph):
+            call()
+    with torch.cuda.stream(stream):
+        graph.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(stream)
+    e1.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (reps * per_graph)
+    del graph
+    nbytes = numel * 4 + cap * 4 + nblk * 4 + 4
+    gbs = nbytes / (us * 1e-6) / 1e9
+    return {"shape": f"topk_ids int32 [{numel // 8}, 8] from the router, {E_} experts, block {bs}",
+            "us_per_call": round(us, 2), "launches_per_call": 3, "algorithmic_bytes": nbytes,
+            "achieved_gbs": round(gbs, 1), "peak_gbs": peak, "frac": round(gbs / peak, 4), "peak_kind": peak_kind}
+
+
 # ---------------------------------------------------------------- ours
 def run_ours(a):
     import numpy as np
@@ -487,6 +540,7 @@ def run_ours(a):
         e2e_ms = max_over_ranks(pg, ev0.elapsed_time(ev1)) / e2e_steps
     del graph
     bw = bandwidth_leg(dev) if "bw" in a.legs else None
+    moe = moe_leg(dev, ids, stream) if "moe" in a.legs else None
     mlp = tp_mlp_leg(rank, world, pg, steps=max(10, min(a.steps, 50)), warmup=3) if "mlp" in a.legs else None
 
     if rank == 0:
@@ -529,6 +583,7 @@ def run_ours(a):
             "gpu_launches": steps,
             "exact_path_rows_per_step": round(exact_per_step, 2),
             "bandwidth_ops": bw,
+            "moe_dispatch": moe,
             "tp_mlp": mlp,
         }
         line["cpu_baseline"] = cpu_baseline(a.cpu_seconds) if (world == 1 and "cpu" in a.legs) else None

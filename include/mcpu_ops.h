@@ -211,6 +211,33 @@ OPENREG_EXPORT orError_t mcpu_mm_allreduce_window_bytes(int64_t M, int64_t N, in
 OPENREG_EXPORT orError_t mcpu_mm_allreduce_control_bytes(uint64_t bytes, int world,
                                                          uint64_t* control_bytes);
 
+/*
+ * moe_align_block_size: MoE expert dispatch after the router, with the
+ * contract of vLLM's op of that name (vllm/_custom_ops.py:2247-2264): the
+ * numel entries of topk_ids (int32 [T, topk] flattened; expert indices in
+ * [0, num_experts), num_experts <= 1024) grouped by expert into
+ * sorted_token_ids, each expert's run in ascending flat index and padded
+ * with the value numel to a multiple of block_size; every slot after the
+ * last run also holds numel.  expert_ids[b] is the expert of slots
+ * [b*block_size, (b+1)*block_size), -1 past the last run;
+ * *num_tokens_post_pad (device int32) the slots the runs fill.
+ * sorted_capacity >= min(numel + num_experts*(block_size-1), numel*block_size),
+ * expert_ids_capacity >= ceil(that / block_size).  workspace: device memory
+ * of mcpu_moe_align_workspace_bytes(numel, num_experts) bytes, no initial
+ * content needed.  Entries outside [0, num_experts) are left out and set
+ * mcpu_device_error.  The reference has no such op: it would assemble the
+ * lists from scatter_add / index ops (csrc/aten/ops/reduction_scatter.cpp:
+ * 517-555) on host views.
+ */
+OPENREG_EXPORT orError_t mcpu_moe_align_block_size(const int32_t* topk_ids, int64_t numel, int num_experts,
+                                                   int block_size, int32_t* sorted_token_ids,
+                                                   int64_t sorted_capacity, int32_t* expert_ids,
+                                                   int64_t expert_ids_capacity, int32_t* num_tokens_post_pad,
+                                                   void* workspace, uint64_t workspace_bytes,
+                                                   orStream_t stream);
+
+OPENREG_EXPORT orError_t mcpu_moe_align_workspace_bytes(int64_t numel, int num_experts, uint64_t* bytes);
+
 /* *flag = 1 if a kernel on the current device (tensor-core GEMM, TMA-fed
  * router or bulk-copy-fed rms_norm) gave up on a bounded wait, or a gather /
  * scatter met an index out of range, since the last reset; that launch left

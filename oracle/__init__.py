@@ -192,3 +192,40 @@ def tp_mlp_bf16(
         y = bf16_bits_to_f32(gemm_bf16(a, wd))
         acc = y if acc is None else acc + y
     return f32_to_bf16_bits(acc)
+
+
+# ---------------------------------------------------------------- MoE dispatch
+def moe_align_block_size(topk_ids: np.ndarray, num_experts: int, block_size: int,
+                         sorted_capacity: int | None = None):
+    """Per-expert token lists after the router, with the contract of vLLM's
+    moe_align_block_size (vllm/_custom_ops.py:2247-2264, documented with a
+    worked example in vllm/model_executor/layers/fused_moe/
+    moe_align_block_size.py:19-73): the flat indices of topk_ids grouped by
+    expert, each expert's run padded with numel to a multiple of block_size.
+    Runs are in ascending flat index (a stable counting sort); slots after the
+    last run hold numel; expert_ids is -1 past the last run; entries outside
+    [0, num_experts) are left out.
+
+    Returns (sorted_token_ids int32 [capacity], expert_ids int32
+    [ceil(capacity / block_size)], num_tokens_post_pad int)."""
+    ids = np.asarray(topk_ids, dtype=np.int64).reshape(-1)
+    numel = ids.size
+    if sorted_capacity is None:
+        sorted_capacity = min(numel + num_experts * (block_size - 1), numel * block_size)
+    valid = (ids >= 0) & (ids < num_experts)
+    counts = np.bincount(ids[valid], minlength=num_experts)
+    padded = (counts + block_size - 1) // block_size * block_size
+    start = np.concatenate([[0], np.cumsum(padded)])
+    out = np.full(sorted_capacity, numel, dtype=np.int32)
+    order = np.nonzero(valid)[0]
+    order = order[np.argsort(ids[order], kind="stable")]
+    pos = 0
+    for e in range(num_experts):
+        c = counts[e]
+        out[start[e]:start[e] + c] = order[pos:pos + c]
+        pos += c
+    nblocks = -(-sorted_capacity // block_size)
+    eids = np.full(nblocks, -1, dtype=np.int32)
+    for e in range(num_experts):
+        eids[start[e] // block_size:start[e + 1] // block_size] = e
+    return out, eids, int(start[-1])

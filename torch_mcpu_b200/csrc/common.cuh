@@ -31,6 +31,7 @@ namespace bw {
 orError_t read_error(int* flag, bool reset);
 }
 orError_t aten_read_error(int* flag, bool reset);
+orError_t moe_read_error(int* flag, bool reset);
 
 inline cudaStream_t as_cuda(orStream_t s) {
   return reinterpret_cast<cudaStream_t>(s);

@@ -1,0 +1,259 @@
+// MoE expert dispatch: the per-expert token lists the fused-MoE GEMMs read,
+// built from the router's topk_ids.  Same contract as vLLM's
+// moe_align_block_size (vllm/_custom_ops.py:2247-2264; documented in
+// vllm/model_executor/layers/fused_moe/moe_align_block_size.py:19-73):
+//   sorted_token_ids  the flat indices i (token * topk + slot) of topk_ids,
+//                     grouped by expert, each expert's run padded with the
+//                     value numel to a multiple of block_size; here every run
+//                     is in ascending i (a stable order), and every slot past
+//                     the last run holds numel as well;
+//   expert_ids        the expert of each block of block_size slots, -1 for
+//                     the blocks past the last run;
+//   num_tokens_post_pad  the number of slots the runs fill.
+// The reference builds such lists, where it needs them, from scatter_add /
+// index ops on host views (csrc/aten/ops/reduction_scatter.cpp:517-555).
+//
+// Three launches over chunks of 4096 entries (one CTA each):
+//   count    per-chunk expert histogram (shared-memory atomics) -> counts
+//   scan     one CTA: expert totals, padded run starts, every chunk's first
+//            slot per expert (written over counts), expert_ids, padding
+//   scatter  per chunk: per-warp histograms, their prefix from the chunk's
+//            slots, then each warp places its 512 entries 32 at a time in
+//            index order (__match_any_sync groups equal experts; rank =
+//            peers below this lane), so runs come out in ascending index.
+// The workspace is the [chunks, experts] int32 matrix; every entry of it is
+// written by the count launch before it is read, so it needs no clearing.
+// Entries outside [0, num_experts) are left out and set the device error
+// flag.
+#include "common.cuh"
+
+namespace mcpu {
+namespace moe {
+
+constexpr int kChunk = 4096;       // entries per chunk (one CTA)
+constexpr int kThreads = 256;      // 8 warps x 512 entries
+constexpr int kWarps = kThreads / 32;
+constexpr int kPerWarp = kChunk / kWarps;
+constexpr int kMaxExperts = 1024;
+constexpr int kScanThreads = 1024;
+
+__device__ int g_moe_error = 0;
+
+__global__ void __launch_bounds__(kThreads) align_count_kernel(const int32_t* __restrict__ ids, long long numel,
+                                                               int E, int32_t* __restrict__ counts) {
+  __shared__ int hist[kMaxExperts];
+  for (int e = threadIdx.x; e < E; e += kThreads) hist[e] = 0;
+  __syncthreads();
+  const long long base = static_cast<long long>(blockIdx.x) * kChunk;
+  const long long left = numel - base;
+  const int n = left < kChunk ? static_cast<int>(left) : kChunk;
+  bool bad = false;
+  for (int i = threadIdx.x; i < n; i += kThreads) {
+    const int e = __ldg(ids + base + i);
+    if (static_cast<unsigned>(e) < static_cast<unsigned>(E))
+      atomicAdd(&hist[e], 1);
+    else
+      bad = true;
+  }
+  if (bad) atomicOr(&g_moe_error, 1);
+  __syncthreads();
+  int32_t* row = counts + static_cast<long long>(blockIdx.x) * E;
+  for (int e = threadIdx.x; e < E; e += kThreads) row[e] = hist[e];
+}
+
+__global__ void __launch_bounds__(kScanThreads) align_scan_kernel(
+    int32_t* __restrict__ counts, int nchunks, int E, int bs, long long numel, int32_t* __restrict__ sorted,
+    long long sorted_cap, int32_t* __restrict__ expert_ids, long long eid_cap, int32_t* __restrict__ post_pad) {
+  __shared__ int part[kScanThreads];        // [P][E] partial totals over chunk ranges
+  __shared__ int start[kMaxExperts + 1];    // padded run starts
+  __shared__ int scan[kScanThreads];
+  const int tid = threadIdx.x;
+  const int P = kScanThreads / E;            // chunk ranges per expert (>= 1)
+  const int e = tid % E, p = tid / E;
+  const bool active = p < P;
+  const int c0 = active ? static_cast<int>(static_cast<long long>(nchunks) * p / P) : 0;
+  const int c1 = active ? static_cast<int>(static_cast<long long>(nchunks) * (p + 1) / P) : 0;
+  int s = 0;
+  for (int c = c0; c < c1; ++c) s += counts[static_cast<long long>(c) * E + e];
+  if (active) part[p * E + e] = s;
+  __syncthreads();
+  // padded totals, exclusive scan over experts
+  int total = 0;
+  if (tid < E)
+    for (int q = 0; q < P; ++q) total += part[q * E + tid];
+  const int padded = tid < E ? (total + bs - 1) / bs * bs : 0;
+  scan[tid] = padded;
+  __syncthreads();
+  for (int off = 1; off < kScanThreads; off <<= 1) {
+    const int v = tid >= off ? scan[tid - off] : 0;
+    __syncthreads();
+    scan[tid] += v;
+    __syncthreads();
+  }
+  if (tid < E) start[tid + 1] = scan[tid];
+  if (tid == 0) start[0] = 0;
+  __syncthreads();
+  const int end = start[E];
+  if (tid == 0) *post_pad = end;
+  // every chunk's first slot per expert
+  if (active) {
+    int run = start[e];
+    for (int q = 0; q < p; ++q) run += part[q * E + e];
+    for (int c = c0; c < c1; ++c) {
+      const long long k = static_cast<long long>(c) * E + e;
+      const int v = counts[k];
+      counts[k] = run;
+      run += v;
+    }
+  }
+  // padding of each run, and every slot past the last run
+  if (tid < E)
+    for (int j = start[tid] + total; j < start[tid + 1]; ++j) sorted[j] = static_cast<int32_t>(numel);
+  for (long long j = end + tid; j < sorted_cap; j += kScanThreads) sorted[j] = static_cast<int32_t>(numel);
+  // the expert of every block (binary search over the run starts)
+  for (long long b = tid; b < eid_cap; b += kScanThreads) {
+    const long long slot = b * bs;
+    int ex = -1;
+    if (slot < end) {
+      int lo = 0, hi = E - 1;  // largest expert whose run starts at or before slot
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (start[mid] <= slot)
+          lo = mid;
+        else
+          hi = mid - 1;
+      }
+      ex = lo;
+    }
+    expert_ids[b] = ex;
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) align_scatter_kernel(const int32_t* __restrict__ ids, long long numel,
+                                                                 int E, const int32_t* __restrict__ first,
+                                                                 int32_t* __restrict__ sorted) {
+  extern __shared__ int whist[];  // [kWarps][E]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i < kWarps * E; i += kThreads) whist[i] = 0;
+  __syncthreads();
+  const long long wbase = static_cast<long long>(blockIdx.x) * kChunk + warp * kPerWarp;
+  int* wh = whist + warp * E;
+  for (int g = 0; g < kPerWarp / 32; ++g) {
+    const long long i = wbase + g * 32 + lane;
+    if (i < numel) {
+      const int e = __ldg(ids + i);
+      if (static_cast<unsigned>(e) < static_cast<unsigned>(E)) atomicAdd(&wh[e], 1);
+    }
+  }
+  __syncthreads();
+  const int32_t* f = first + static_cast<long long>(blockIdx.x) * E;
+  for (int e = threadIdx.x; e < E; e += kThreads) {
+    int run = f[e];
+    for (int w = 0; w < kWarps; ++w) {
+      const int c = whist[w * E + e];
+      whist[w * E + e] = run;
+      run += c;
+    }
+  }
+  __syncthreads();
+  const unsigned below = (1u << lane) - 1u;
+  for (int g = 0; g < kPerWarp / 32; ++g) {
+    const long long i = wbase + g * 32 + lane;
+    int e = -1;
+    if (i < numel) {
+      e = __ldg(ids + i);
+      if (static_cast<unsigned>(e) >= static_cast<unsigned>(E)) e = -1;
+    }
+    const unsigned peers = __match_any_sync(0xFFFFFFFFu, e);
+    const int rank = __popc(peers & below);
+    if (e >= 0) sorted[wh[e] + rank] = static_cast<int32_t>(i);
+    __syncwarp();
+    if (e >= 0 && rank == 0) wh[e] += __popc(peers);
+    __syncwarp();
+  }
+}
+
+// Checks shared by the entry points; *nchunks_out = chunks of the input.
+orError_t check_args(const int32_t* topk_ids, long long numel, int E, int bs, const int32_t* sorted,
+                     long long sorted_cap, const int32_t* expert_ids, long long eid_cap, const int32_t* post_pad,
+                     int* nchunks_out) {
+  MCPU_ARG_CHECK(numel >= 0 && numel < (1LL << 31), "moe_align_block_size: numel %lld out of range", numel);
+  MCPU_ARG_CHECK(E >= 1 && E <= kMaxExperts, "moe_align_block_size: num_experts %d outside 1..%d", E,
+                 kMaxExperts);
+  MCPU_ARG_CHECK(bs >= 1 && bs <= (1 << 20), "moe_align_block_size: block_size %d out of range", bs);
+  MCPU_ARG_CHECK(sorted && expert_ids && post_pad, "moe_align_block_size: NULL output");
+  MCPU_ARG_CHECK(numel == 0 || topk_ids, "moe_align_block_size: NULL topk_ids");
+  const long long a = numel + static_cast<long long>(E) * (bs - 1), b = numel * bs;
+  const long long min_cap = a < b ? a : b;
+  MCPU_ARG_CHECK(sorted_cap >= min_cap && sorted_cap < (1LL << 31),
+                 "moe_align_block_size: sorted_token_ids holds %lld entries, %lld needed", sorted_cap, min_cap);
+  MCPU_ARG_CHECK(eid_cap >= (min_cap + bs - 1) / bs,
+                 "moe_align_block_size: expert_ids holds %lld entries, %lld needed", eid_cap,
+                 (min_cap + bs - 1) / bs);
+  *nchunks_out = static_cast<int>((numel + kChunk - 1) / kChunk);
+  return orSuccess;
+}
+
+// The three launches, with `counts` as the [chunks, E] workspace.
+orError_t launch(const int32_t* topk_ids, long long numel, int E, int bs, int32_t* sorted, long long sorted_cap,
+                 int32_t* expert_ids, long long eid_cap, int32_t* post_pad, int32_t* counts, int nchunks,
+                 cudaStream_t st) {
+  if (nchunks > 0) {
+    align_count_kernel<<<nchunks, kThreads, 0, st>>>(topk_ids, numel, E, counts);
+    MCPU_CUDA_TRY(cudaGetLastError(), "moe_align_block_size count launch");
+  }
+  align_scan_kernel<<<1, kScanThreads, 0, st>>>(counts, nchunks, E, bs, numel, sorted, sorted_cap, expert_ids,
+                                                eid_cap, post_pad);
+  MCPU_CUDA_TRY(cudaGetLastError(), "moe_align_block_size scan launch");
+  if (nchunks > 0) {
+    align_scatter_kernel<<<nchunks, kThreads, kWarps * E * 4, st>>>(topk_ids, numel, E, counts, sorted);
+    MCPU_CUDA_TRY(cudaGetLastError(), "moe_align_block_size scatter launch");
+  }
+  return orSuccess;
+}
+
+}  // namespace moe
+
+orError_t moe_read_error(int* flag, bool reset) {
+  MCPU_CUDA_TRY(cudaMemcpyFromSymbol(flag, moe::g_moe_error, sizeof(int)), "moe error flag");
+  if (reset) {
+    const int zero = 0;
+    MCPU_CUDA_TRY(cudaMemcpyToSymbol(moe::g_moe_error, &zero, sizeof(int)), "moe error flag reset");
+  }
+  return orSuccess;
+}
+
+}  // namespace mcpu
+
+using namespace mcpu;
+
+extern "C" orError_t mcpu_moe_align_workspace_bytes(int64_t numel, int num_experts, uint64_t* bytes) {
+  MCPU_ARG_CHECK(bytes != nullptr, "moe_align_block_size: NULL output");
+  MCPU_ARG_CHECK(numel >= 0 && numel < (1LL << 31), "moe_align_block_size: numel %lld out of range",
+                 static_cast<long long>(numel));
+  MCPU_ARG_CHECK(num_experts >= 1 && num_experts <= moe::kMaxExperts,
+                 "moe_align_block_size: num_experts %d outside 1..%d", num_experts, moe::kMaxExperts);
+  const long long nchunks = (numel + moe::kChunk - 1) / moe::kChunk;
+  *bytes = static_cast<uint64_t>((nchunks > 0 ? nchunks : 1) * num_experts * 4);
+  return orSuccess;
+}
+
+extern "C" orError_t mcpu_moe_align_block_size(const int32_t* topk_ids, int64_t numel, int num_experts,
+                                               int block_size, int32_t* sorted_token_ids,
+                                               int64_t sorted_capacity, int32_t* expert_ids,
+                                               int64_t expert_ids_capacity, int32_t* num_tokens_post_pad,
+                                               void* workspace, uint64_t workspace_bytes, orStream_t stream) {
+  int nchunks = 0;
+  orError_t e = moe::check_args(topk_ids, numel, num_experts, block_size, sorted_token_ids, sorted_capacity,
+                                expert_ids, expert_ids_capacity, num_tokens_post_pad, &nchunks);
+  if (e != orSuccess) return e;
+  uint64_t need = 0;
+  e = mcpu_moe_align_workspace_bytes(numel, num_experts, &need);
+  if (e != orSuccess) return e;
+  MCPU_ARG_CHECK(workspace != nullptr && workspace_bytes >= need,
+                 "moe_align_block_size: workspace of %llu bytes, %llu needed",
+                 static_cast<unsigned long long>(workspace_bytes), static_cast<unsigned long long>(need));
+  return moe::launch(topk_ids, numel, num_experts, block_size, sorted_token_ids, sorted_capacity, expert_ids,
+                     expert_ids_capacity, num_tokens_post_pad, static_cast<int32_t*>(workspace), nchunks,
+                     as_cuda(stream));
+}

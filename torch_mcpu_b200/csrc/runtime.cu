@@ -118,10 +118,12 @@ orError_t mcpu_device_error(int* flag, int reset) {
   if (e != orSuccess) return e;
   e = bw::read_error(&c, reset != 0);
   if (e != orSuccess) return e;
-  int d = 0;
+  int d = 0, m = 0;
   e = aten_read_error(&d, reset != 0);
   if (e != orSuccess) return e;
-  *flag = a | b | c | d;
+  e = moe_read_error(&m, reset != 0);
+  if (e != orSuccess) return e;
+  *flag = a | b | c | d | m;
   return orSuccess;
 }
 

@@ -612,6 +612,30 @@ at::Tensor gemm_swiglu(const at::Tensor& x, const at::Tensor& w_gate_up) {
   return gemm_swiglu_out(a, w, out);
 }
 
+// MoE expert dispatch after the router, vLLM's moe_align_block_size schema
+// (vllm/_custom_ops.py:2247-2264); the workspace comes from the device's
+// stream-ordered allocator.
+void moe_align_block_size(const at::Tensor& topk_ids, int64_t num_experts, int64_t block_size,
+                          at::Tensor& sorted_token_ids, at::Tensor& experts_ids, at::Tensor& num_tokens_post_pad) {
+  TORCH_CHECK(topk_ids.scalar_type() == at::kInt || topk_ids.scalar_type() == at::kLong,
+              "moe_align_block_size: topk_ids must be int32 or int64");
+  for (const at::Tensor* t : {&sorted_token_ids, &experts_ids, &num_tokens_post_pad}) {
+    TORCH_CHECK(t->scalar_type() == at::kInt && t->is_contiguous() && t->device() == topk_ids.device(),
+                "moe_align_block_size: outputs must be contiguous int32 tensors on the ids' device");
+  }
+  TORCH_CHECK(num_tokens_post_pad.numel() >= 1, "moe_align_block_size: num_tokens_post_pad needs one element");
+  const at::Tensor ids = topk_ids.to(at::kInt).contiguous();
+  uint64_t ws = 0;
+  MCPU_OK(mcpu_moe_align_workspace_bytes(ids.numel(), static_cast<int>(num_experts), &ws),
+          "moe_align_block_size");
+  at::Tensor work = at::empty({static_cast<int64_t>(ws)}, ids.options().dtype(at::kByte));
+  MCPU_OK(mcpu_moe_align_block_size(ids.const_data_ptr<int32_t>(), ids.numel(), static_cast<int>(num_experts),
+                                    static_cast<int>(block_size), sorted_token_ids.data_ptr<int32_t>(),
+                                    sorted_token_ids.numel(), experts_ids.data_ptr<int32_t>(), experts_ids.numel(),
+                                    num_tokens_post_pad.data_ptr<int32_t>(), work.data_ptr(), ws, stream_of(ids)),
+          "moe_align_block_size");
+}
+
 // Row-parallel down projection + SUM all-reduce of the partials in one kernel
 // (mm, csrc/aten/ops/mm.cpp:13-51, then McpuBackend::allreduce,
 // torch_mcpu/csrc/Distributed.cpp:403-413).  `window` is the address of the
@@ -711,6 +735,8 @@ TORCH_LIBRARY_FRAGMENT(mcpu, m) {
   m.def("gemm_swiglu(Tensor x, Tensor w_gate_up_interleaved) -> Tensor");
   m.def("gemm_swiglu.out(Tensor x, Tensor w_gate_up_interleaved, *, Tensor(a!) out) -> Tensor(a!)");
   m.def("mm_allreduce(Tensor a, Tensor b, int window) -> Tensor");
+  m.def("moe_align_block_size(Tensor topk_ids, int num_experts, int block_size, Tensor(a!) sorted_token_ids, "
+        "Tensor(b!) experts_ids, Tensor(c!) num_tokens_post_pad) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(mcpu, PrivateUse1, m) {
@@ -721,4 +747,5 @@ TORCH_LIBRARY_IMPL(mcpu, PrivateUse1, m) {
   m.impl("gemm_swiglu", gemm_swiglu);
   m.impl("gemm_swiglu.out", gemm_swiglu_out);
   m.impl("mm_allreduce", mm_allreduce);
+  m.impl("moe_align_block_size", moe_align_block_size);
 }

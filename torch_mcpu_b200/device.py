@@ -259,11 +259,13 @@ def init() -> None:
 
 
 def manual_seed(seed: int) -> None:
-    torch.manual_seed(seed)  # mcpu tensors are drawn on the host, then copied
+    # mcpu tensors are drawn by the host generator, then copied; torch.manual_seed
+    # itself calls manual_seed_all of this module, so seed the generator directly
+    torch.default_generator.manual_seed(int(seed))
 
 
 def manual_seed_all(seed: int) -> None:
-    torch.manual_seed(seed)
+    torch.default_generator.manual_seed(int(seed))
 
 
 def _is_in_bad_fork() -> bool:

@@ -178,6 +178,40 @@ def gemm_swiglu(x: torch.Tensor, w_gate_up_interleaved: torch.Tensor,
     return out
 
 
+def moe_align_block_size(topk_ids: torch.Tensor, block_size: int, num_experts: int,
+                         expert_map: torch.Tensor | None = None, pad_sorted_ids: bool = False):
+    """Per-expert token lists for the fused-MoE GEMMs, with the signature and
+    outputs of vLLM's moe_align_block_size
+    (vllm/model_executor/layers/fused_moe/moe_align_block_size.py:11-18):
+    (sorted_token_ids, expert_ids, num_tokens_post_pad).  Runs are in
+    ascending flat index; slots after the last run hold numel and blocks past
+    it have expert -1."""
+    import ctypes
+
+    _require_device(topk_ids, "topk_ids")
+    if expert_map is not None:
+        raise NotImplementedError("moe_align_block_size: expert_map is not supported")
+    ids = topk_ids.to(torch.int32).contiguous()
+    numel = ids.numel()
+    cap = min(numel + num_experts * (block_size - 1), numel * block_size)
+    if pad_sorted_ids:
+        cap = -(-cap // block_size) * block_size
+    nblocks = -(-cap // block_size)
+    dev = ids.device
+    sorted_ids = torch.empty(max(cap, 1), dtype=torch.int32, device=dev)[:cap]
+    expert_ids = torch.empty(max(nblocks, 1), dtype=torch.int32, device=dev)[:nblocks]
+    post_pad = torch.empty(1, dtype=torch.int32, device=dev)
+    lib = _lib.load()
+    ws = ctypes.c_uint64()
+    _lib.check(lib.mcpu_moe_align_workspace_bytes(numel, num_experts, ctypes.byref(ws)), "moe_align_block_size")
+    work = torch.empty(ws.value, dtype=torch.uint8, device=dev)
+    _lib.check(lib.mcpu_moe_align_block_size(ids.data_ptr(), numel, num_experts, block_size, sorted_ids.data_ptr(),
+                                             sorted_ids.numel(), expert_ids.data_ptr(), expert_ids.numel(),
+                                             post_pad.data_ptr(), work.data_ptr(), ws.value, _stream_handle(dev)),
+               "moe_align_block_size")
+    return sorted_ids, expert_ids, post_pad
+
+
 def device_error(reset: bool = False) -> int:
     """1 if a kernel gave up on a bounded wait since the last reset."""
     import ctypes
