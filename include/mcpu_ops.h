@@ -238,6 +238,29 @@ OPENREG_EXPORT orError_t mcpu_moe_align_block_size(const int32_t* topk_ids, int6
 
 OPENREG_EXPORT orError_t mcpu_moe_align_workspace_bytes(int64_t numel, int num_experts, uint64_t* bytes);
 
+/*
+ * moe_align_block_size_static: the same dispatch, for callers that cannot
+ * allocate device memory when they dispatch experts -- an inference engine
+ * that reserved all free memory for its own pool at start-up, code that must
+ * not stall on cudaMalloc's device-wide synchronisation while serving, or a
+ * C caller with no device allocator.  No workspace argument: the count
+ * matrix lives in a fixed 256 KiB array of this library's device memory
+ * (65536 int32 counters, kept on every GPU that loads the library until the
+ * process exits), so ceil(numel / 4096) * num_experts must be <= 65536 --
+ * up to 1,048,576 entries with 256 experts; larger calls fail with
+ * orErrorInvalidValue and a message naming the limit.  It allocates nothing
+ * and calls no allocating routine.  The first call on each device looks up
+ * the array's device address (cudaGetSymbolAddress) on the current device;
+ * make that first call before any stream capture.  All calls share the
+ * array: calls whose kernels overlap on the GPU race, so order them on one
+ * stream.  No counterpart in the reference.
+ */
+OPENREG_EXPORT orError_t mcpu_moe_align_block_size_static(const int32_t* topk_ids, int64_t numel, int num_experts,
+                                                          int block_size, int32_t* sorted_token_ids,
+                                                          int64_t sorted_capacity, int32_t* expert_ids,
+                                                          int64_t expert_ids_capacity,
+                                                          int32_t* num_tokens_post_pad, orStream_t stream);
+
 /* *flag = 1 if a kernel on the current device (tensor-core GEMM, TMA-fed
  * router or bulk-copy-fed rms_norm) gave up on a bounded wait, or a gather /
  * scatter met an index out of range, since the last reset; that launch left

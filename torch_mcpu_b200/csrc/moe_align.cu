@@ -25,6 +25,8 @@
 // written by the count launch before it is read, so it needs no clearing.
 // Entries outside [0, num_experts) are left out and set the device error
 // flag.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace mcpu {
@@ -256,4 +258,79 @@ extern "C" orError_t mcpu_moe_align_block_size(const int32_t* topk_ids, int64_t 
   return moe::launch(topk_ids, numel, num_experts, block_size, sorted_token_ids, sorted_capacity, expert_ids,
                      expert_ids_capacity, num_tokens_post_pad, static_cast<int32_t*>(workspace), nchunks,
                      as_cuda(stream));
+}
+
+// ---------------------------------------------------------------------------
+// The same dispatch without any allocation.
+//
+// Some callers cannot hand this op a workspace: an inference engine that
+// reserved all free device memory for its own pool when it started (a
+// cudaMalloc then fails, or fragments memory the engine manages itself),
+// code that must not trigger cudaMalloc's device-wide synchronisation in
+// the middle of serving, and plain C callers with no device allocator of
+// their own.  mcpu_moe_align_block_size_static keeps the [chunks, experts]
+// count matrix in a fixed array of this library's own device memory
+// instead: 65536 int32 counters (256 KiB, held on every GPU that loads the
+// library until the process exits), enough for chunks x experts <= 65536,
+// e.g. 1,048,576 entries (131072 tokens at top-8) with 256 experts.  Larger
+// problems are rejected with an error; they need the workspace entry point.
+//
+// Nothing in the array has to start at zero: the count launch writes every
+// counter the later launches read.  Every call shares the one array, so two
+// calls whose kernels overlap on the GPU (other streams, other host
+// threads) race on it; order them on one stream.
+namespace {
+
+constexpr long long kStaticCounters = 65536;
+static __device__ __align__(256) int32_t g_moe_static_counts[kStaticCounters];
+
+// Device address of the array on the current device.  In host code the
+// array's name is only a host-side stand-in, so the address is looked up
+// with cudaGetSymbolAddress once per device (on that device's first call)
+// and kept.
+constexpr int kMaxDevices = 64;
+std::mutex g_static_mutex;
+int32_t* g_static_addr[kMaxDevices] = {};
+
+orError_t static_counts_address(int32_t** out) {
+  int dev = 0;
+  MCPU_CUDA_TRY(cudaGetDevice(&dev), "moe_align_block_size_static: cudaGetDevice");
+  MCPU_ARG_CHECK(dev >= 0 && dev < kMaxDevices, "moe_align_block_size_static: device %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_static_mutex);
+  if (g_static_addr[dev] == nullptr) {
+    void* p = nullptr;
+    MCPU_CUDA_TRY(cudaGetSymbolAddress(&p, g_moe_static_counts), "moe_align_block_size_static: cudaGetSymbolAddress");
+    MCPU_ARG_CHECK(p != nullptr, "moe_align_block_size_static: no device address for the fixed scratch");
+    g_static_addr[dev] = static_cast<int32_t*>(p);
+  }
+  *out = g_static_addr[dev];
+  return orSuccess;
+}
+
+}  // namespace
+
+extern "C" orError_t mcpu_moe_align_block_size_static(const int32_t* topk_ids, int64_t numel, int num_experts,
+                                                      int block_size, int32_t* sorted_token_ids,
+                                                      int64_t sorted_capacity, int32_t* expert_ids,
+                                                      int64_t expert_ids_capacity, int32_t* num_tokens_post_pad,
+                                                      orStream_t stream) {
+  uint64_t need_bytes = 0;
+  orError_t e = mcpu_moe_align_workspace_bytes(numel, num_experts, &need_bytes);  // validates numel, experts
+  if (e != orSuccess) return e;
+  const long long need = static_cast<long long>(need_bytes / 4);
+  MCPU_ARG_CHECK(need <= kStaticCounters,
+                 "moe_align_block_size_static: %lld entries over %d experts need %lld counters, the fixed "
+                 "scratch holds %lld (at most %lld entries for this expert count); use mcpu_moe_align_block_size "
+                 "with a workspace",
+                 static_cast<long long>(numel), num_experts, need, kStaticCounters,
+                 kStaticCounters / num_experts * moe::kChunk);
+  int nchunks = 0;
+  e = moe::check_args(topk_ids, numel, num_experts, block_size, sorted_token_ids, sorted_capacity, expert_ids,
+                      expert_ids_capacity, num_tokens_post_pad, &nchunks);
+  if (e != orSuccess) return e;
+  int32_t* counts = nullptr;
+  e = static_counts_address(&counts);
+  if (e != orSuccess) return e;
+  return moe::launch(topk_ids, numel, num_experts, block_size, sorted_token_ids, sorted_capacity, expert_ids,
+                     expert_ids_capacity, num_tokens_post_pad, counts, nchunks, as_cuda(stream));
 }
