@@ -13,16 +13,19 @@
 // The reference builds such lists, where it needs them, from scatter_add /
 // index ops on host views (csrc/aten/ops/reduction_scatter.cpp:517-555).
 //
-// Three launches over chunks of 4096 entries (one CTA each):
+// Three launches over chunks of 4096 entries (one 1024-thread CTA each):
 //   count    per-chunk expert histogram (shared-memory atomics) -> counts
 //   scan     one CTA: expert totals, padded run starts, every chunk's first
-//            slot per expert (written over counts), expert_ids, padding
+//            slot per expert (written over counts)
 //   scatter  per chunk: per-warp histograms, their prefix from the chunk's
-//            slots, then each warp places its 512 entries 32 at a time in
+//            slots, then each warp places its 128 entries 32 at a time in
 //            index order (__match_any_sync groups equal experts; rank =
-//            peers below this lane), so runs come out in ascending index.
-// The workspace is the [chunks, experts] int32 matrix; every entry of it is
-// written by the count launch before it is read, so it needs no clearing.
+//            peers below this lane), so runs come out in ascending index;
+//            then the grid writes the run padding, the slots after the last
+//            run and the expert of every block.
+// The workspace is the [chunks, experts] int32 matrix plus two rows (run
+// starts, entry counts); every entry of it is written before it is read, so
+// it needs no clearing.
 // Entries outside [0, num_experts) are left out and set the device error
 // flag.
 #include <mutex>
@@ -33,13 +36,17 @@ namespace mcpu {
 namespace moe {
 
 constexpr int kChunk = 4096;       // entries per chunk (one CTA)
-constexpr int kThreads = 256;      // 8 warps x 512 entries
+constexpr int kThreads = 1024;     // 32 warps x 128 entries
 constexpr int kWarps = kThreads / 32;
 constexpr int kPerWarp = kChunk / kWarps;
 constexpr int kMaxExperts = 1024;
 constexpr int kScanThreads = 1024;
 
 __device__ int g_moe_error = 0;
+
+// Workspace ints for nchunks chunks: the [nchunks, E] count matrix, then
+// the padded run start and the entry count of every expert.
+inline long long workspace_ints(long long nchunks, int E) { return (nchunks + 2) * E; }
 
 __global__ void __launch_bounds__(kThreads) align_count_kernel(const int32_t* __restrict__ ids, long long numel,
                                                                int E, int32_t* __restrict__ counts) {
@@ -50,10 +57,17 @@ __global__ void __launch_bounds__(kThreads) align_count_kernel(const int32_t* __
   const long long left = numel - base;
   const int n = left < kChunk ? static_cast<int>(left) : kChunk;
   bool bad = false;
-  for (int i = threadIdx.x; i < n; i += kThreads) {
-    const int e = __ldg(ids + base + i);
-    if (static_cast<unsigned>(e) < static_cast<unsigned>(E))
-      atomicAdd(&hist[e], 1);
+  int ev[kChunk / kThreads];
+#pragma unroll
+  for (int k = 0; k < kChunk / kThreads; ++k) {  // all loads in flight first
+    const int i = threadIdx.x + k * kThreads;
+    ev[k] = i < n ? __ldg(ids + base + i) : 0;
+  }
+#pragma unroll
+  for (int k = 0; k < kChunk / kThreads; ++k) {
+    if (threadIdx.x + k * kThreads >= n) continue;
+    if (static_cast<unsigned>(ev[k]) < static_cast<unsigned>(E))
+      atomicAdd(&hist[ev[k]], 1);
     else
       bad = true;
   }
@@ -63,28 +77,28 @@ __global__ void __launch_bounds__(kThreads) align_count_kernel(const int32_t* __
   for (int e = threadIdx.x; e < E; e += kThreads) row[e] = hist[e];
 }
 
-__global__ void __launch_bounds__(kScanThreads) align_scan_kernel(
-    int32_t* __restrict__ counts, int nchunks, int E, int bs, long long numel, int32_t* __restrict__ sorted,
-    long long sorted_cap, int32_t* __restrict__ expert_ids, long long eid_cap, int32_t* __restrict__ post_pad) {
-  __shared__ int part[kScanThreads];        // [P][E] partial totals over chunk ranges
-  __shared__ int start[kMaxExperts + 1];    // padded run starts
+// One CTA: expert totals, padded run starts (exclusive scan), and every
+// chunk's first slot per expert written over the counts.  Run starts and
+// totals go to the two rows after the counts; the slot count to *post_pad.
+__global__ void __launch_bounds__(kScanThreads) align_scan_kernel(int32_t* __restrict__ counts, int nchunks,
+                                                                  int E, int bs, int32_t* __restrict__ post_pad) {
+  __shared__ int part[kScanThreads];  // [P][E] partial totals over chunk ranges
   __shared__ int scan[kScanThreads];
   const int tid = threadIdx.x;
-  const int P = kScanThreads / E;            // chunk ranges per expert (>= 1)
+  const int P = kScanThreads / E;      // chunk ranges per expert (>= 1)
   const int e = tid % E, p = tid / E;
   const bool active = p < P;
   const int c0 = active ? static_cast<int>(static_cast<long long>(nchunks) * p / P) : 0;
   const int c1 = active ? static_cast<int>(static_cast<long long>(nchunks) * (p + 1) / P) : 0;
   int s = 0;
+#pragma unroll 8
   for (int c = c0; c < c1; ++c) s += counts[static_cast<long long>(c) * E + e];
   if (active) part[p * E + e] = s;
   __syncthreads();
-  // padded totals, exclusive scan over experts
   int total = 0;
   if (tid < E)
     for (int q = 0; q < P; ++q) total += part[q * E + tid];
-  const int padded = tid < E ? (total + bs - 1) / bs * bs : 0;
-  scan[tid] = padded;
+  scan[tid] = tid < E ? (total + bs - 1) / bs * bs : 0;
   __syncthreads();
   for (int off = 1; off < kScanThreads; off <<= 1) {
     const int v = tid >= off ? scan[tid - off] : 0;
@@ -92,28 +106,103 @@ __global__ void __launch_bounds__(kScanThreads) align_scan_kernel(
     scan[tid] += v;
     __syncthreads();
   }
-  if (tid < E) start[tid + 1] = scan[tid];
-  if (tid == 0) start[0] = 0;
-  __syncthreads();
-  const int end = start[E];
-  if (tid == 0) *post_pad = end;
-  // every chunk's first slot per expert
+  int32_t* starts = counts + static_cast<long long>(nchunks) * E;
+  int32_t* totals = starts + E;
+  if (tid < E) {
+    starts[tid] = tid == 0 ? 0 : scan[tid - 1];
+    totals[tid] = total;
+  }
+  if (tid == kScanThreads - 1) *post_pad = scan[kScanThreads - 1];
   if (active) {
-    int run = start[e];
+    int run = e == 0 ? 0 : scan[e - 1];
     for (int q = 0; q < p; ++q) run += part[q * E + e];
-    for (int c = c0; c < c1; ++c) {
+    int c = c0;
+    for (; c + 8 <= c1; c += 8) {  // eight loads in flight, then eight stores
+      int v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = counts[static_cast<long long>(c + u) * E + e];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        counts[static_cast<long long>(c + u) * E + e] = run;
+        run += v[u];
+      }
+    }
+    for (; c < c1; ++c) {
       const long long k = static_cast<long long>(c) * E + e;
       const int v = counts[k];
       counts[k] = run;
       run += v;
     }
   }
-  // padding of each run, and every slot past the last run
-  if (tid < E)
-    for (int j = start[tid] + total; j < start[tid + 1]; ++j) sorted[j] = static_cast<int32_t>(numel);
-  for (long long j = end + tid; j < sorted_cap; j += kScanThreads) sorted[j] = static_cast<int32_t>(numel);
-  // the expert of every block (binary search over the run starts)
-  for (long long b = tid; b < eid_cap; b += kScanThreads) {
+}
+
+// One CTA per chunk (at least one CTA): places the chunk's entries, then
+// the grid shares the rest of the outputs: the padding of each run, every
+// slot after the last run, and the expert of every block.
+__global__ void __launch_bounds__(kThreads) align_scatter_kernel(
+    const int32_t* __restrict__ ids, long long numel, int nchunks, int E, int bs, const int32_t* __restrict__ ws,
+    const int32_t* __restrict__ post_pad, int32_t* __restrict__ sorted, long long sorted_cap,
+    int32_t* __restrict__ expert_ids, long long eid_cap) {
+  extern __shared__ int smem[];  // [kWarps][E] per-warp slots, then [E + 1] run starts
+  int* whist = smem;
+  int* start = smem + kWarps * E;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int32_t* starts = ws + static_cast<long long>(nchunks) * E;
+  const int32_t* totals = starts + E;
+  const int end = *post_pad;
+  for (int i = threadIdx.x; i < E; i += kThreads) start[i] = starts[i];
+  if (threadIdx.x == 0) start[E] = end;
+  if (blockIdx.x < nchunks) {
+    for (int i = threadIdx.x; i < kWarps * E; i += kThreads) whist[i] = 0;
+    __syncthreads();
+    const long long wbase = static_cast<long long>(blockIdx.x) * kChunk + warp * kPerWarp;
+    int* wh = whist + warp * E;
+    int ev[kPerWarp / 32];  // this lane's entries, loaded once (-1: none or out of range)
+#pragma unroll
+    for (int g = 0; g < kPerWarp / 32; ++g) {
+      const long long i = wbase + g * 32 + lane;
+      int e = i < numel ? __ldg(ids + i) : -1;
+      if (static_cast<unsigned>(e) >= static_cast<unsigned>(E)) e = -1;
+      ev[g] = e;
+    }
+#pragma unroll
+    for (int g = 0; g < kPerWarp / 32; ++g)
+      if (ev[g] >= 0) atomicAdd(&wh[ev[g]], 1);
+    __syncthreads();
+    const int32_t* f = ws + static_cast<long long>(blockIdx.x) * E;
+    for (int e = threadIdx.x; e < E; e += kThreads) {
+      int run = f[e];
+      for (int w = 0; w < kWarps; ++w) {
+        const int c = whist[w * E + e];
+        whist[w * E + e] = run;
+        run += c;
+      }
+    }
+    __syncthreads();
+    const unsigned below = (1u << lane) - 1u;
+#pragma unroll
+    for (int g = 0; g < kPerWarp / 32; ++g) {
+      const long long i = wbase + g * 32 + lane;
+      const int e = ev[g];
+      const unsigned peers = __match_any_sync(0xFFFFFFFFu, e);
+      const int rank = __popc(peers & below);
+      if (e >= 0) sorted[wh[e] + rank] = static_cast<int32_t>(i);
+      __syncwarp();
+      if (e >= 0 && rank == 0) wh[e] += __popc(peers);
+      __syncwarp();
+    }
+  } else {
+    __syncthreads();  // start[] staged
+  }
+  // padding of runs: expert e by CTA e % grid
+  for (int e = blockIdx.x; e < E; e += gridDim.x) {
+    const int from = start[e] + totals[e], to = start[e + 1];
+    for (int j = from + threadIdx.x; j < to; j += kThreads) sorted[j] = static_cast<int32_t>(numel);
+  }
+  const long long gtid = static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x;
+  const long long gthreads = static_cast<long long>(gridDim.x) * kThreads;
+  for (long long j = end + gtid; j < sorted_cap; j += gthreads) sorted[j] = static_cast<int32_t>(numel);
+  for (long long b = gtid; b < eid_cap; b += gthreads) {
     const long long slot = b * bs;
     int ex = -1;
     if (slot < end) {
@@ -128,50 +217,6 @@ __global__ void __launch_bounds__(kScanThreads) align_scan_kernel(
       ex = lo;
     }
     expert_ids[b] = ex;
-  }
-}
-
-__global__ void __launch_bounds__(kThreads) align_scatter_kernel(const int32_t* __restrict__ ids, long long numel,
-                                                                 int E, const int32_t* __restrict__ first,
-                                                                 int32_t* __restrict__ sorted) {
-  extern __shared__ int whist[];  // [kWarps][E]
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int i = threadIdx.x; i < kWarps * E; i += kThreads) whist[i] = 0;
-  __syncthreads();
-  const long long wbase = static_cast<long long>(blockIdx.x) * kChunk + warp * kPerWarp;
-  int* wh = whist + warp * E;
-  for (int g = 0; g < kPerWarp / 32; ++g) {
-    const long long i = wbase + g * 32 + lane;
-    if (i < numel) {
-      const int e = __ldg(ids + i);
-      if (static_cast<unsigned>(e) < static_cast<unsigned>(E)) atomicAdd(&wh[e], 1);
-    }
-  }
-  __syncthreads();
-  const int32_t* f = first + static_cast<long long>(blockIdx.x) * E;
-  for (int e = threadIdx.x; e < E; e += kThreads) {
-    int run = f[e];
-    for (int w = 0; w < kWarps; ++w) {
-      const int c = whist[w * E + e];
-      whist[w * E + e] = run;
-      run += c;
-    }
-  }
-  __syncthreads();
-  const unsigned below = (1u << lane) - 1u;
-  for (int g = 0; g < kPerWarp / 32; ++g) {
-    const long long i = wbase + g * 32 + lane;
-    int e = -1;
-    if (i < numel) {
-      e = __ldg(ids + i);
-      if (static_cast<unsigned>(e) >= static_cast<unsigned>(E)) e = -1;
-    }
-    const unsigned peers = __match_any_sync(0xFFFFFFFFu, e);
-    const int rank = __popc(peers & below);
-    if (e >= 0) sorted[wh[e] + rank] = static_cast<int32_t>(i);
-    __syncwarp();
-    if (e >= 0 && rank == 0) wh[e] += __popc(peers);
-    __syncwarp();
   }
 }
 
@@ -196,21 +241,27 @@ orError_t check_args(const int32_t* topk_ids, long long numel, int E, int bs, co
   return orSuccess;
 }
 
-// The three launches, with `counts` as the [chunks, E] workspace.
+// The three launches, with `ws` as the workspace (workspace_ints ints).
 orError_t launch(const int32_t* topk_ids, long long numel, int E, int bs, int32_t* sorted, long long sorted_cap,
-                 int32_t* expert_ids, long long eid_cap, int32_t* post_pad, int32_t* counts, int nchunks,
+                 int32_t* expert_ids, long long eid_cap, int32_t* post_pad, int32_t* ws, int nchunks,
                  cudaStream_t st) {
+  const int smem = (kWarps * E + E + 1) * 4;
+  static std::once_flag attr_once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(attr_once, [] {
+    attr_err = cudaFuncSetAttribute(align_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (kWarps * kMaxExperts + kMaxExperts + 1) * 4);
+  });
+  MCPU_CUDA_TRY(attr_err, "moe_align_block_size scatter attribute");
   if (nchunks > 0) {
-    align_count_kernel<<<nchunks, kThreads, 0, st>>>(topk_ids, numel, E, counts);
+    align_count_kernel<<<nchunks, kThreads, 0, st>>>(topk_ids, numel, E, ws);
     MCPU_CUDA_TRY(cudaGetLastError(), "moe_align_block_size count launch");
   }
-  align_scan_kernel<<<1, kScanThreads, 0, st>>>(counts, nchunks, E, bs, numel, sorted, sorted_cap, expert_ids,
-                                                eid_cap, post_pad);
+  align_scan_kernel<<<1, kScanThreads, 0, st>>>(ws, nchunks, E, bs, post_pad);
   MCPU_CUDA_TRY(cudaGetLastError(), "moe_align_block_size scan launch");
-  if (nchunks > 0) {
-    align_scatter_kernel<<<nchunks, kThreads, kWarps * E * 4, st>>>(topk_ids, numel, E, counts, sorted);
-    MCPU_CUDA_TRY(cudaGetLastError(), "moe_align_block_size scatter launch");
-  }
+  align_scatter_kernel<<<nchunks > 0 ? nchunks : 1, kThreads, smem, st>>>(
+      topk_ids, numel, nchunks, E, bs, ws, post_pad, sorted, sorted_cap, expert_ids, eid_cap);
+  MCPU_CUDA_TRY(cudaGetLastError(), "moe_align_block_size scatter launch");
   return orSuccess;
 }
 
@@ -236,7 +287,7 @@ extern "C" orError_t mcpu_moe_align_workspace_bytes(int64_t numel, int num_exper
   MCPU_ARG_CHECK(num_experts >= 1 && num_experts <= moe::kMaxExperts,
                  "moe_align_block_size: num_experts %d outside 1..%d", num_experts, moe::kMaxExperts);
   const long long nchunks = (numel + moe::kChunk - 1) / moe::kChunk;
-  *bytes = static_cast<uint64_t>((nchunks > 0 ? nchunks : 1) * num_experts * 4);
+  *bytes = static_cast<uint64_t>(moe::workspace_ints(nchunks, num_experts) * 4);
   return orSuccess;
 }
 
@@ -271,8 +322,9 @@ extern "C" orError_t mcpu_moe_align_block_size(const int32_t* topk_ids, int64_t 
 // their own.  mcpu_moe_align_block_size_static keeps the [chunks, experts]
 // count matrix in a fixed array of this library's own device memory
 // instead: 65536 int32 counters (256 KiB, held on every GPU that loads the
-// library until the process exits), enough for chunks x experts <= 65536,
-// e.g. 1,048,576 entries (131072 tokens at top-8) with 256 experts.  Larger
+// library until the process exits), enough for (chunks + 2) x experts <=
+// 65536 with 4096-entry chunks, e.g. 1,040,384 entries (130048 tokens at
+// top-8) with 256 experts.  Larger
 // problems are rejected with an error; they need the workspace entry point.
 //
 // Nothing in the array has to start at zero: the count launch writes every
@@ -323,7 +375,7 @@ extern "C" orError_t mcpu_moe_align_block_size_static(const int32_t* topk_ids, i
                  "scratch holds %lld (at most %lld entries for this expert count); use mcpu_moe_align_block_size "
                  "with a workspace",
                  static_cast<long long>(numel), num_experts, need, kStaticCounters,
-                 kStaticCounters / num_experts * moe::kChunk);
+                 (kStaticCounters / num_experts - 2) * moe::kChunk);
   int nchunks = 0;
   e = moe::check_args(topk_ids, numel, num_experts, block_size, sorted_token_ids, sorted_capacity, expert_ids,
                       expert_ids_capacity, num_tokens_post_pad, &nchunks);
