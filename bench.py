@@ -421,7 +421,7 @@ def moe_leg(dev, ids, stream, reps=8, per_graph=32):
     nbytes = numel * 4 + cap * 4 + nblk * 4 + 4
     gbs = nbytes / (us * 1e-6) / 1e9
     return {"shape": f"topk_ids int32 [{numel // 8}, 8] from the router, {E_} experts, block {bs}",
-            "us_per_call": round(us, 2), "launches_per_call": 3, "algorithmic_bytes": nbytes,
+            "us_per_call": round(us, 2), "launches_per_call": 2, "algorithmic_bytes": nbytes,
             "achieved_gbs": round(gbs, 1), "peak_gbs": peak, "frac": round(gbs / peak, 4), "peak_kind": peak_kind}
 
 

@@ -246,8 +246,8 @@ OPENREG_EXPORT orError_t mcpu_moe_align_workspace_bytes(int64_t numel, int num_e
  * C caller with no device allocator.  No workspace argument: the count
  * matrix lives in a fixed 256 KiB array of this library's device memory
  * (65536 int32 counters, kept on every GPU that loads the library until the
- * process exits), so (ceil(numel / 4096) + 2) * num_experts must be <=
- * 65536 -- up to 1,040,384 entries with 256 experts; larger calls fail with
+ * process exits), so ceil(numel / 4096) * num_experts must be <= 65536 --
+ * up to 1,048,576 entries with 256 experts; larger calls fail with
  * orErrorInvalidValue and a message naming the limit.  It allocates nothing
  * and calls no allocating routine.  The first call on each device looks up
  * the array's device address (cudaGetSymbolAddress) on the current device;

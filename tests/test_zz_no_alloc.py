@@ -75,7 +75,7 @@ def test_static_scratch_entry_point_refuses_problems_beyond_its_limit():
     lib = _lib.load()
     ids = torch.zeros(8, dtype=torch.int32, device="cuda")
     out = torch.zeros(8, dtype=torch.int32, device="cuda")
-    numel = 4096 * 255  # (255 + 2) chunks x 256 experts > 65536 counters; refused before any launch
+    numel = 4096 * 257  # 257 chunks x 256 experts > 65536 counters; refused before any launch
     rc = lib.mcpu_moe_align_block_size_static(ids.data_ptr(), numel, 256, 64, out.data_ptr(), out.numel(),
                                               out.data_ptr(), out.numel(), out.data_ptr(),
                                               torch.cuda.current_stream().cuda_stream)

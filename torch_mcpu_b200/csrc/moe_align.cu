@@ -13,19 +13,20 @@
 // The reference builds such lists, where it needs them, from scatter_add /
 // index ops on host views (csrc/aten/ops/reduction_scatter.cpp:517-555).
 //
-// Three launches over chunks of 4096 entries (one 1024-thread CTA each):
+// Two launches over chunks of 4096 entries (one 1024-thread CTA each):
 //   count    per-chunk expert histogram (shared-memory atomics) -> counts
-//   scan     one CTA: expert totals, padded run starts, every chunk's first
-//            slot per expert (written over counts)
-//   scatter  per chunk: per-warp histograms, their prefix from the chunk's
-//            slots, then each warp places its 128 entries 32 at a time in
-//            index order (__match_any_sync groups equal experts; rank =
-//            peers below this lane), so runs come out in ascending index;
-//            then the grid writes the run padding, the slots after the last
-//            run and the expert of every block.
-// The workspace is the [chunks, experts] int32 matrix plus two rows (run
-// starts, entry counts); every entry of it is written before it is read, so
-// it needs no clearing.
+//   scatter  per chunk: reads every chunk's histogram (L2) for the expert
+//            totals and the entries of the chunks before it, scans the
+//            padded totals into run starts, builds per-warp histograms and
+//            their prefix from the chunk's first slots, then each warp
+//            places its 128 entries 32 at a time in index order
+//            (__match_any_sync groups equal experts; rank = peers below
+//            this lane), so runs come out in ascending index; then the grid
+//            writes the run padding, the slots after the last run and the
+//            expert of every block.
+// The workspace is the [chunks, experts] int32 count matrix; every entry of
+// it is written by the count launch before it is read, so it needs no
+// clearing.
 // Entries outside [0, num_experts) are left out and set the device error
 // flag.
 #include <mutex>
@@ -40,13 +41,12 @@ constexpr int kThreads = 1024;     // 32 warps x 128 entries
 constexpr int kWarps = kThreads / 32;
 constexpr int kPerWarp = kChunk / kWarps;
 constexpr int kMaxExperts = 1024;
-constexpr int kScanThreads = 1024;
 
 __device__ int g_moe_error = 0;
 
-// Workspace ints for nchunks chunks: the [nchunks, E] count matrix, then
-// the padded run start and the entry count of every expert.
-inline long long workspace_ints(long long nchunks, int E) { return (nchunks + 2) * E; }
+// Workspace ints for nchunks chunks: the [nchunks, E] count matrix (at
+// least one row).
+inline long long workspace_ints(long long nchunks, int E) { return (nchunks > 0 ? nchunks : 1) * E; }
 
 __global__ void __launch_bounds__(kThreads) align_count_kernel(const int32_t* __restrict__ ids, long long numel,
                                                                int E, int32_t* __restrict__ counts) {
@@ -77,85 +77,80 @@ __global__ void __launch_bounds__(kThreads) align_count_kernel(const int32_t* __
   for (int e = threadIdx.x; e < E; e += kThreads) row[e] = hist[e];
 }
 
-// One CTA: expert totals, padded run starts (exclusive scan), and every
-// chunk's first slot per expert written over the counts.  Run starts and
-// totals go to the two rows after the counts; the slot count to *post_pad.
-__global__ void __launch_bounds__(kScanThreads) align_scan_kernel(int32_t* __restrict__ counts, int nchunks,
-                                                                  int E, int bs, int32_t* __restrict__ post_pad) {
-  __shared__ int part[kScanThreads];  // [P][E] partial totals over chunk ranges
-  __shared__ int scan[kScanThreads];
-  const int tid = threadIdx.x;
-  const int P = kScanThreads / E;      // chunk ranges per expert (>= 1)
-  const int e = tid % E, p = tid / E;
-  const bool active = p < P;
-  const int c0 = active ? static_cast<int>(static_cast<long long>(nchunks) * p / P) : 0;
-  const int c1 = active ? static_cast<int>(static_cast<long long>(nchunks) * (p + 1) / P) : 0;
-  int s = 0;
-#pragma unroll 8
-  for (int c = c0; c < c1; ++c) s += counts[static_cast<long long>(c) * E + e];
-  if (active) part[p * E + e] = s;
+// One CTA per chunk (at least one CTA).  Every CTA reads the whole count
+// matrix (all chunks' histograms, from L2) for the expert totals and for the
+// entries of its own earlier chunks, scans the padded totals into run starts,
+// places its chunk's entries, then the grid shares the rest of the outputs:
+// the padding of each run, every slot after the last run, the expert of
+// every block and (CTA 0) the slot count.
+__global__ void __launch_bounds__(kThreads) align_scatter_kernel(
+    const int32_t* __restrict__ ids, long long numel, int nchunks, int E, int bs,
+    const int32_t* __restrict__ counts, int32_t* __restrict__ post_pad, int32_t* __restrict__ sorted,
+    long long sorted_cap, int32_t* __restrict__ expert_ids, long long eid_cap) {
+  extern __shared__ int smem[];  // [kWarps][E] per-warp slots | [E + 1] run starts | [P][E] x 2 partials
+  int* whist = smem;
+  int* start = whist + kWarps * E;
+  int* ptot = start + E + 1;
+  int* pbef = ptot + kThreads;
+  __shared__ int scan[kThreads];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int me = blockIdx.x;
+  // expert totals and the entries of chunks before this one: P threads per
+  // expert, each over every P-th chunk
+  const int P = kThreads / E;  // >= 1
+  {
+    const int e = tid % E, q = tid / E;
+    int tot = 0, bef = 0;
+    if (q < P) {
+      int c = q;
+      for (; c + 7 * P < nchunks; c += 8 * P) {  // eight loads in flight
+        int v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[u] = counts[static_cast<long long>(c + u * P) * E + e];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          tot += v[u];
+          bef += c + u * P < me ? v[u] : 0;
+        }
+      }
+      for (; c < nchunks; c += P) {
+        const int v = counts[static_cast<long long>(c) * E + e];
+        tot += v;
+        bef += c < me ? v : 0;
+      }
+      ptot[q * E + e] = tot;
+      pbef[q * E + e] = bef;
+    }
+  }
   __syncthreads();
-  int total = 0;
-  if (tid < E)
-    for (int q = 0; q < P; ++q) total += part[q * E + tid];
+  int total = 0, before = 0;
+  if (tid < E) {
+    for (int q = 0; q < P; ++q) {
+      total += ptot[q * E + tid];
+      before += pbef[q * E + tid];
+    }
+  }
   scan[tid] = tid < E ? (total + bs - 1) / bs * bs : 0;
   __syncthreads();
-  for (int off = 1; off < kScanThreads; off <<= 1) {
+  for (int off = 1; off < kThreads; off <<= 1) {
     const int v = tid >= off ? scan[tid - off] : 0;
     __syncthreads();
     scan[tid] += v;
     __syncthreads();
   }
-  int32_t* starts = counts + static_cast<long long>(nchunks) * E;
-  int32_t* totals = starts + E;
-  if (tid < E) {
-    starts[tid] = tid == 0 ? 0 : scan[tid - 1];
-    totals[tid] = total;
-  }
-  if (tid == kScanThreads - 1) *post_pad = scan[kScanThreads - 1];
-  if (active) {
-    int run = e == 0 ? 0 : scan[e - 1];
-    for (int q = 0; q < p; ++q) run += part[q * E + e];
-    int c = c0;
-    for (; c + 8 <= c1; c += 8) {  // eight loads in flight, then eight stores
-      int v[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) v[u] = counts[static_cast<long long>(c + u) * E + e];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        counts[static_cast<long long>(c + u) * E + e] = run;
-        run += v[u];
-      }
-    }
-    for (; c < c1; ++c) {
-      const long long k = static_cast<long long>(c) * E + e;
-      const int v = counts[k];
-      counts[k] = run;
-      run += v;
-    }
-  }
-}
-
-// One CTA per chunk (at least one CTA): places the chunk's entries, then
-// the grid shares the rest of the outputs: the padding of each run, every
-// slot after the last run, and the expert of every block.
-__global__ void __launch_bounds__(kThreads) align_scatter_kernel(
-    const int32_t* __restrict__ ids, long long numel, int nchunks, int E, int bs, const int32_t* __restrict__ ws,
-    const int32_t* __restrict__ post_pad, int32_t* __restrict__ sorted, long long sorted_cap,
-    int32_t* __restrict__ expert_ids, long long eid_cap) {
-  extern __shared__ int smem[];  // [kWarps][E] per-warp slots, then [E + 1] run starts
-  int* whist = smem;
-  int* start = smem + kWarps * E;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int32_t* starts = ws + static_cast<long long>(nchunks) * E;
-  const int32_t* totals = starts + E;
-  const int end = *post_pad;
-  for (int i = threadIdx.x; i < E; i += kThreads) start[i] = starts[i];
-  if (threadIdx.x == 0) start[E] = end;
-  if (blockIdx.x < nchunks) {
-    for (int i = threadIdx.x; i < kWarps * E; i += kThreads) whist[i] = 0;
+  const int end = scan[kThreads - 1];
+  if (tid < E) start[tid] = tid == 0 ? 0 : scan[tid - 1];
+  if (tid == 0) start[E] = end;
+  if (me == 0 && tid == 0) *post_pad = end;
+  // this chunk's first slot per expert, kept in the per-warp table of warp 0's
+  // position until the per-warp prefix below
+  int first = 0;
+  if (tid < E) first = (tid == 0 ? 0 : scan[tid - 1]) + before;
+  __syncthreads();
+  if (me < nchunks) {
+    for (int i = tid; i < kWarps * E; i += kThreads) whist[i] = 0;
     __syncthreads();
-    const long long wbase = static_cast<long long>(blockIdx.x) * kChunk + warp * kPerWarp;
+    const long long wbase = static_cast<long long>(me) * kChunk + warp * kPerWarp;
     int* wh = whist + warp * E;
     int ev[kPerWarp / 32];  // this lane's entries, loaded once (-1: none or out of range)
 #pragma unroll
@@ -169,12 +164,11 @@ __global__ void __launch_bounds__(kThreads) align_scatter_kernel(
     for (int g = 0; g < kPerWarp / 32; ++g)
       if (ev[g] >= 0) atomicAdd(&wh[ev[g]], 1);
     __syncthreads();
-    const int32_t* f = ws + static_cast<long long>(blockIdx.x) * E;
-    for (int e = threadIdx.x; e < E; e += kThreads) {
-      int run = f[e];
+    if (tid < E) {
+      int run = first;
       for (int w = 0; w < kWarps; ++w) {
-        const int c = whist[w * E + e];
-        whist[w * E + e] = run;
+        const int c = whist[w * E + tid];
+        whist[w * E + tid] = run;
         run += c;
       }
     }
@@ -191,15 +185,15 @@ __global__ void __launch_bounds__(kThreads) align_scatter_kernel(
       if (e >= 0 && rank == 0) wh[e] += __popc(peers);
       __syncwarp();
     }
-  } else {
-    __syncthreads();  // start[] staged
   }
-  // padding of runs: expert e by CTA e % grid
-  for (int e = blockIdx.x; e < E; e += gridDim.x) {
-    const int from = start[e] + totals[e], to = start[e + 1];
-    for (int j = from + threadIdx.x; j < to; j += kThreads) sorted[j] = static_cast<int32_t>(numel);
+  // padding of runs: expert e by CTA e % grid (its totals are in ptot/start)
+  for (int e = me; e < E; e += gridDim.x) {
+    int tot = 0;
+    for (int q = 0; q < P; ++q) tot += ptot[q * E + e];
+    const int from = start[e] + tot, to = start[e + 1];
+    for (int j = from + tid; j < to; j += kThreads) sorted[j] = static_cast<int32_t>(numel);
   }
-  const long long gtid = static_cast<long long>(blockIdx.x) * kThreads + threadIdx.x;
+  const long long gtid = static_cast<long long>(me) * kThreads + tid;
   const long long gthreads = static_cast<long long>(gridDim.x) * kThreads;
   for (long long j = end + gtid; j < sorted_cap; j += gthreads) sorted[j] = static_cast<int32_t>(numel);
   for (long long b = gtid; b < eid_cap; b += gthreads) {
@@ -241,24 +235,22 @@ orError_t check_args(const int32_t* topk_ids, long long numel, int E, int bs, co
   return orSuccess;
 }
 
-// The three launches, with `ws` as the workspace (workspace_ints ints).
+// The two launches, with `ws` as the [chunks, E] count workspace.
 orError_t launch(const int32_t* topk_ids, long long numel, int E, int bs, int32_t* sorted, long long sorted_cap,
                  int32_t* expert_ids, long long eid_cap, int32_t* post_pad, int32_t* ws, int nchunks,
                  cudaStream_t st) {
-  const int smem = (kWarps * E + E + 1) * 4;
+  const int smem = (kWarps * E + E + 1 + 2 * kThreads) * 4;
   static std::once_flag attr_once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(attr_once, [] {
     attr_err = cudaFuncSetAttribute(align_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    (kWarps * kMaxExperts + kMaxExperts + 1) * 4);
+                                    (kWarps * kMaxExperts + kMaxExperts + 1 + 2 * kThreads) * 4);
   });
   MCPU_CUDA_TRY(attr_err, "moe_align_block_size scatter attribute");
   if (nchunks > 0) {
     align_count_kernel<<<nchunks, kThreads, 0, st>>>(topk_ids, numel, E, ws);
     MCPU_CUDA_TRY(cudaGetLastError(), "moe_align_block_size count launch");
   }
-  align_scan_kernel<<<1, kScanThreads, 0, st>>>(ws, nchunks, E, bs, post_pad);
-  MCPU_CUDA_TRY(cudaGetLastError(), "moe_align_block_size scan launch");
   align_scatter_kernel<<<nchunks > 0 ? nchunks : 1, kThreads, smem, st>>>(
       topk_ids, numel, nchunks, E, bs, ws, post_pad, sorted, sorted_cap, expert_ids, eid_cap);
   MCPU_CUDA_TRY(cudaGetLastError(), "moe_align_block_size scatter launch");
@@ -322,9 +314,9 @@ extern "C" orError_t mcpu_moe_align_block_size(const int32_t* topk_ids, int64_t 
 // their own.  mcpu_moe_align_block_size_static keeps the [chunks, experts]
 // count matrix in a fixed array of this library's own device memory
 // instead: 65536 int32 counters (256 KiB, held on every GPU that loads the
-// library until the process exits), enough for (chunks + 2) x experts <=
-// 65536 with 4096-entry chunks, e.g. 1,040,384 entries (130048 tokens at
-// top-8) with 256 experts.  Larger
+// library until the process exits), enough for chunks x experts <= 65536
+// with 4096-entry chunks, e.g. 1,048,576 entries (131072 tokens at top-8)
+// with 256 experts.  Larger
 // problems are rejected with an error; they need the workspace entry point.
 //
 // Nothing in the array has to start at zero: the count launch writes every
@@ -375,7 +367,7 @@ extern "C" orError_t mcpu_moe_align_block_size_static(const int32_t* topk_ids, i
                  "scratch holds %lld (at most %lld entries for this expert count); use mcpu_moe_align_block_size "
                  "with a workspace",
                  static_cast<long long>(numel), num_experts, need, kStaticCounters,
-                 (kStaticCounters / num_experts - 2) * moe::kChunk);
+                 kStaticCounters / num_experts * moe::kChunk);
   int nchunks = 0;
   e = moe::check_args(topk_ids, numel, num_experts, block_size, sorted_token_ids, sorted_capacity, expert_ids,
                       expert_ids_capacity, num_tokens_post_pad, &nchunks);
