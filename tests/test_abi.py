@@ -90,3 +90,21 @@ def test_extension_exports_the_launch_api():
     out = subprocess.run(["nm", "-DC", "--defined-only", build_ext.SO], capture_output=True, text=True).stdout
     missing = [w for w in wanted if not re.search(r"\b" + w + r"\b", out)]
     assert not missing, missing
+
+
+def test_extension_shares_libstdcxx_with_torch():
+    """The torch extension must use the process's libstdc++ (dynamically),
+    not a private static copy: torch formats its error messages with its own
+    streams, and a second copy of the stream code crashes on them."""
+    import shutil
+    import subprocess
+
+    from torch_mcpu_b200 import build_ext
+
+    if shutil.which("readelf") is None:
+        pytest.skip("readelf not available")
+    so = build_ext.build()
+    dyn = subprocess.run(["readelf", "-d", so], capture_output=True, text=True).stdout
+    assert "libstdc++.so" in dyn
+    syms = subprocess.run(["readelf", "--dyn-syms", "-W", so], capture_output=True, text=True).stdout
+    assert "_ZNKSt19__codecvt_utf8_baseIwE10do_unshift" not in syms  # libstdc++ internals not linked in

@@ -42,10 +42,25 @@ def up_to_date() -> bool:
     return os.path.getmtime(SO) >= max(os.path.getmtime(f) for f in deps)
 
 
+def _use_shared_libstdcxx_compiler() -> None:
+    """The extension has to share libstdc++ with torch: a private static copy
+    (what a toolchain gives when its shared libstdc++ cannot be found) has its
+    own iostream and locale objects, and torch's error messages, formatted
+    with torch's streams, then crash when they print a number.  The system
+    g++ links libstdc++ dynamically, so it builds the extension when present."""
+    for cxx, cc in (("/usr/bin/g++", "/usr/bin/gcc"),):
+        if os.path.exists(cxx):
+            os.environ["CXX"] = cxx
+            if os.path.exists(cc):
+                os.environ["CC"] = cc
+            return
+
+
 def build(verbose: bool = False) -> str:
     _cabi.build()
     if up_to_date():
         return SO
+    _use_shared_libstdcxx_compiler()
     from torch.utils import cpp_extension
 
     nccl_inc, nccl_lib = _nccl_dirs()
@@ -81,6 +96,7 @@ def build_launch_check(verbose: bool = False) -> str:
     deps = [CHECK_SRC, SO, os.path.join(ROOT, "include", "mcpu_launch.h")]
     if os.path.exists(CHECK_SO) and os.path.getmtime(CHECK_SO) >= max(os.path.getmtime(f) for f in deps):
         return CHECK_SO
+    _use_shared_libstdcxx_compiler()
     from torch.utils import cpp_extension
 
     cpp_extension.load(
