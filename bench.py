@@ -56,8 +56,8 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="bound on the host-core baseline's sampling time")
-    ap.add_argument("--legs", default="e2e,bw,moe,mlp,cpu",
-                    help="extra legs besides the router timing (comma list of e2e, bw, moe, mlp, cpu; "
+    ap.add_argument("--legs", default="e2e,bw,moe,sampler,mlp,cpu",
+                    help="extra legs besides the router timing (comma list of e2e, bw, moe, sampler, mlp, cpu; "
                          "'none' for the router alone, e.g. under a profiler)")
     a = ap.parse_args()
     a.legs = set() if a.legs == "none" else set(a.legs.split(","))
@@ -425,6 +425,53 @@ def moe_leg(dev, ids, stream, reps=8, per_graph=32):
             "achieved_gbs": round(gbs, 1), "peak_gbs": peak, "frac": round(gbs / peak, 4), "peak_kind": peak_kind}
 
 
+def sampler_leg(dev, reps=20):
+    """The reference's vLLM sampler ops on a decode batch: 256 rows x 128256
+    vocab fp32 logits (131 MB, more than L2): min_p in place (p = 0.05 on
+    every row) and top-5 log-probabilities; CUDA-event time per call and
+    GB/s of the algorithmic bytes (the logits read once; each row's second
+    pass re-reads it from L2)."""
+    import torch
+
+    from torch_mcpu_b200 import _lib
+
+    lib = _lib.load()
+    peak, peak_kind = measured_peaks()
+    rows, vocab = 256, 128256
+    g = torch.Generator(device=dev).manual_seed(9)
+    xs = [3.0 * torch.randn(rows, vocab, generator=g, device=dev) for _ in range(2)]
+    idx = torch.arange(rows, dtype=torch.int32, device=dev)
+    mp = torch.full((rows,), 0.05, dtype=torch.float32, device=dev)
+    ids = torch.randint(0, vocab, (rows, 5), device=dev, generator=g)
+    out = torch.empty(rows, 5, dtype=torch.float32, device=dev)
+    s = torch.cuda.current_stream(dev).cuda_stream
+    cases = [
+        ("vllm_min_p", rows * vocab * 4,
+         lambda i: _lib.check(lib.mcpu_vllm_min_p(xs[i % 2].data_ptr(), 0, rows, vocab, idx.data_ptr(),
+                                                  mp.data_ptr(), vocab, s), "min_p")),
+        ("vllm_topk_log_softmax", rows * vocab * 4,
+         lambda i: _lib.check(lib.mcpu_vllm_topk_log_softmax(out.data_ptr(), xs[i % 2].data_ptr(), 0, rows, vocab,
+                                                             ids.data_ptr(), 5, 5, vocab, s), "log_softmax")),
+    ]
+    res = {}
+    for name, nbytes, fn in cases:
+        for i in range(3):
+            fn(i)
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(reps):
+            fn(i)
+        e1.record()
+        e1.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / reps
+        gbs = nbytes / (us * 1e-6) / 1e9
+        res[name] = {"shape": f"logits fp32 [{rows}, {vocab}]", "us_per_call": round(us, 2),
+                     "algorithmic_bytes": nbytes, "achieved_gbs": round(gbs, 1), "peak_gbs": peak,
+                     "frac": round(gbs / peak, 4), "peak_kind": peak_kind}
+    return res
+
+
 # ---------------------------------------------------------------- ours
 def run_ours(a):
     import numpy as np
@@ -541,6 +588,7 @@ def run_ours(a):
     del graph
     bw = bandwidth_leg(dev) if "bw" in a.legs else None
     moe = moe_leg(dev, ids, stream) if "moe" in a.legs else None
+    sampler = sampler_leg(dev) if "sampler" in a.legs else None
     mlp = tp_mlp_leg(rank, world, pg, steps=max(10, min(a.steps, 50)), warmup=3) if "mlp" in a.legs else None
 
     if rank == 0:
@@ -584,6 +632,7 @@ def run_ours(a):
             "exact_path_rows_per_step": round(exact_per_step, 2),
             "bandwidth_ops": bw,
             "moe_dispatch": moe,
+            "sampler_ops": sampler,
             "tp_mlp": mlp,
         }
         line["cpu_baseline"] = cpu_baseline(a.cpu_seconds) if (world == 1 and "cpu" in a.legs) else None

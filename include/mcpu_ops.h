@@ -261,6 +261,34 @@ OPENREG_EXPORT orError_t mcpu_moe_align_block_size_static(const int32_t* topk_id
                                                           int64_t expert_ids_capacity,
                                                           int32_t* num_tokens_post_pad, orStream_t stream);
 
+/*
+ * vLLM sampler kernels of the decode path, the reference's own mcpu ops
+ * (csrc/aten/vllm_kernels/min_p.cpp, logprob.cpp; schemas
+ * mcpu::vllm_min_p_kernel, vllm_topk_log_softmax_kernel, vllm_ranks_kernel).
+ * logits: [rows, logits_stride] on the device, float32 / float16 / bfloat16
+ * (dtype code), the first vocab_size columns used; values compared as fp32.
+ *
+ * min_p (min_p.cpp:13-58): for each token row, min_p[expanded_idx_mapping[t]]
+ *   = p; p == 0 leaves the row; else entries < rowmax + logf(p) become -inf,
+ *   in place.
+ * topk_log_softmax (logprob.cpp:15-69): output[r, k] (fp32, [batch, topk]) =
+ *   logits[r, id] - (rowmax + log(sum exp(x - rowmax))), the sum in fp64, id =
+ *   topk_ids[r, k] (int64, row stride topk_ids_stride) clamped to the vocab.
+ * ranks (logprob.cpp:123-149): output[r] (int64) = number of entries >=
+ *   logits[r, token_ids[r]]; a token id outside the vocab gives 0 and sets
+ *   mcpu_device_error (the reference reads out of bounds).
+ */
+OPENREG_EXPORT orError_t mcpu_vllm_min_p(void* logits, int dtype, int64_t num_tokens, int64_t logits_stride,
+                                         const int32_t* expanded_idx_mapping, const float* min_p,
+                                         int64_t vocab_size, orStream_t stream);
+OPENREG_EXPORT orError_t mcpu_vllm_topk_log_softmax(float* output, const void* logits, int dtype, int64_t batch,
+                                                    int64_t logits_stride, const int64_t* topk_ids,
+                                                    int64_t topk_ids_stride, int64_t topk, int64_t vocab_size,
+                                                    orStream_t stream);
+OPENREG_EXPORT orError_t mcpu_vllm_ranks(int64_t* output, const void* logits, int dtype, int64_t batch,
+                                         int64_t logits_stride, const int64_t* token_ids, int64_t vocab_size,
+                                         orStream_t stream);
+
 /* *flag = 1 if a kernel on the current device (tensor-core GEMM, TMA-fed
  * router or bulk-copy-fed rms_norm) gave up on a bounded wait, or a gather /
  * scatter met an index out of range, since the last reset; that launch left

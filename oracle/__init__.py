@@ -229,3 +229,51 @@ def moe_align_block_size(topk_ids: np.ndarray, num_experts: int, block_size: int
     for e in range(num_experts):
         eids[start[e] // block_size:start[e + 1] // block_size] = e
     return out, eids, int(start[-1])
+
+
+# ---------------------------------------------------------------- sampler
+def _row_max_ref(row: np.ndarray) -> np.float32:
+    # a running `x > max` from -inf: NaN never becomes the maximum
+    finite = row[~np.isnan(row)]
+    return np.float32(finite.max()) if finite.size else np.float32(-np.inf)
+
+
+def vllm_min_p(logits: np.ndarray, idx: np.ndarray, min_p: np.ndarray, vocab: int) -> np.ndarray:
+    """min_p.cpp:13-58 of the reference: per token row, with p =
+    min_p[idx[t]], p == 0 leaves the row; else every entry (as fp32) below
+    rowmax + logf(p) becomes -inf.  logits: fp32 values of the rows (exact
+    for fp16/bf16 inputs); returns the new fp32 values."""
+    out = np.array(logits, dtype=np.float32, copy=True)
+    for t in range(out.shape[0]):
+        p = np.float32(min_p[idx[t]])
+        if p == 0:
+            continue
+        row = out[t, :vocab]
+        with np.errstate(invalid="ignore", divide="ignore"):
+            thr = np.float32(_row_max_ref(row) + np.float32(np.log(np.float64(p))))
+            row[row < thr] = -np.inf
+    return out
+
+
+def vllm_topk_log_softmax(logits: np.ndarray, ids: np.ndarray, vocab: int) -> np.ndarray:
+    """logprob.cpp:15-69: out[r, k] = logits[r, id] - lse, lse = max +
+    (float)log(sum exp((double)(x - max))), id clamped to [0, vocab)."""
+    lg = np.asarray(logits, dtype=np.float32)
+    out = np.empty(ids.shape, dtype=np.float32)
+    for r in range(lg.shape[0]):
+        row = lg[r, :vocab]
+        m = _row_max_ref(row)
+        with np.errstate(invalid="ignore", over="ignore"):
+            se = np.exp((row - m).astype(np.float64)).sum()
+            lse = np.float32(m + np.float32(np.log(se)))
+        for k in range(ids.shape[1]):
+            i = min(max(int(ids[r, k]), 0), vocab - 1)
+            out[r, k] = np.float32(row[i] - lse)
+    return out
+
+
+def vllm_ranks(logits: np.ndarray, token_ids: np.ndarray, vocab: int) -> np.ndarray:
+    """logprob.cpp:123-149: out[r] = number of entries >= logits[r, token]."""
+    lg = np.asarray(logits, dtype=np.float32)
+    return np.array([int((lg[r, :vocab] >= lg[r, int(token_ids[r])]).sum()) for r in range(lg.shape[0])],
+                    dtype=np.int64)

@@ -32,6 +32,7 @@ orError_t read_error(int* flag, bool reset);
 }
 orError_t aten_read_error(int* flag, bool reset);
 orError_t moe_read_error(int* flag, bool reset);
+orError_t sampler_read_error(int* flag, bool reset);
 
 inline cudaStream_t as_cuda(orStream_t s) {
   return reinterpret_cast<cudaStream_t>(s);

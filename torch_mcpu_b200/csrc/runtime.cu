@@ -123,7 +123,10 @@ orError_t mcpu_device_error(int* flag, int reset) {
   if (e != orSuccess) return e;
   e = moe_read_error(&m, reset != 0);
   if (e != orSuccess) return e;
-  *flag = a | b | c | d | m;
+  int sp = 0;
+  e = sampler_read_error(&sp, reset != 0);
+  if (e != orSuccess) return e;
+  *flag = a | b | c | d | m | sp;
   return orSuccess;
 }
 

@@ -1,0 +1,261 @@
+// vLLM sampler kernels the reference registers on the mcpu device
+// (csrc/aten/vllm_kernels/min_p.cpp, logprob.cpp), which run after the model
+// on the decode path:
+//   vllm_min_p_kernel             logits below max + log(min_p) -> -inf, in
+//                                 place, per token's request (min_p.cpp:13-58)
+//   vllm_topk_log_softmax_kernel  logits[ids] - logsumexp(row)
+//                                 (logprob.cpp:15-69)
+//   vllm_ranks_kernel             number of logits >= the sampled token's
+//                                 (logprob.cpp:123-149)
+// One 1024-thread CTA per row: a pass for the row maximum (16-byte loads
+// where the row allows), then the op's pass over the row again (from L2).
+// Logits are fp32, fp16 or bf16, compared as fp32 like the reference; the
+// log-sum-exp accumulates exp(x - max) in fp64 as the reference does.
+#include <math.h>
+
+#include "common.cuh"
+
+namespace mcpu {
+namespace sampler {
+
+constexpr int kThreads = 1024;
+
+__device__ int g_sampler_error = 0;
+
+template <typename T>
+__device__ __forceinline__ float to_f(T v);
+template <>
+__device__ __forceinline__ float to_f<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float to_f<__half>(__half v) { return __half2float(v); }
+template <>
+__device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+template <typename T>
+__device__ __forceinline__ T neg_inf();
+template <>
+__device__ __forceinline__ float neg_inf<float>() { return -INFINITY; }
+template <>
+__device__ __forceinline__ __half neg_inf<__half>() { return __ushort_as_half(0xFC00); }
+template <>
+__device__ __forceinline__ __nv_bfloat16 neg_inf<__nv_bfloat16>() { return __ushort_as_bfloat16(0xFF80); }
+
+// Calls f(i, value) for every element of the row: 16-byte vectors when the
+// row start is 16-byte aligned, scalars for the rest.
+template <typename T, typename F>
+__device__ __forceinline__ void for_row(const T* row, long long n, F&& f) {
+  constexpr int V = 16 / sizeof(T);
+  long long head = 0;
+  if ((reinterpret_cast<uintptr_t>(row) & 15) == 0) {
+    const long long nv = n / V;
+    const uint4* rv = reinterpret_cast<const uint4*>(row);
+    long long j = threadIdx.x;
+    for (; j + 3 * kThreads < nv; j += 4 * kThreads) {  // four 16-byte loads in flight per thread
+      uint4 u[4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) u[r] = __ldg(rv + j + r * kThreads);
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const T* t = reinterpret_cast<const T*>(&u[r]);
+#pragma unroll
+        for (int k = 0; k < V; ++k) f((j + r * kThreads) * V + k, to_f(t[k]));
+      }
+    }
+    for (; j < nv; j += kThreads) {
+      const uint4 u = __ldg(rv + j);
+      const T* t = reinterpret_cast<const T*>(&u);
+#pragma unroll
+      for (int k = 0; k < V; ++k) f(j * V + k, to_f(t[k]));
+    }
+    head = nv * V;
+  }
+  for (long long i = head + threadIdx.x; i < n; i += kThreads) f(i, to_f(row[i]));
+}
+
+__device__ __forceinline__ float block_max(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  v = l < kThreads / 32 ? red[l] : -INFINITY;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
+  return v;
+}
+
+template <typename A>
+__device__ __forceinline__ A block_sum(A v, A* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  v = l < kThreads / 32 ? red[l] : A(0);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+  return v;
+}
+
+// The row maximum as the reference takes it: a running `v > max` from -inf,
+// so NaN never becomes the maximum.
+template <typename T>
+__device__ __forceinline__ float row_max(const T* row, long long n, float* red) {
+  float m = -INFINITY;
+  for_row(row, n, [&](long long, float v) { m = v > m ? v : m; });
+  return block_max(m, red);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads) min_p_kernel(T* logits, long long stride, const int32_t* idx,
+                                                         const float* min_p, long long vocab) {
+  __shared__ float red[kThreads / 32];
+  T* row = logits + blockIdx.x * stride;
+  const float mp = min_p[idx[blockIdx.x]];
+  if (mp == 0.0f) return;
+  // log(p) rounded once from fp64: the fp32 logarithm to within rounding
+  const float thr = row_max(row, vocab, red) + static_cast<float>(log(static_cast<double>(mp)));
+  for_row(static_cast<const T*>(row), vocab, [&](long long i, float v) {
+    if (v < thr) row[i] = neg_inf<T>();
+  });
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads) topk_log_softmax_kernel(float* out, const T* logits, long long stride,
+                                                                    const int64_t* ids, long long ids_stride,
+                                                                    int topk, long long vocab) {
+  __shared__ float red[kThreads / 32];
+  __shared__ double redd[kThreads / 32];
+  const T* row = logits + blockIdx.x * stride;
+  const float m = row_max(row, vocab, red);
+  double s = 0.0;
+  for_row(row, vocab, [&](long long, float v) { s += exp(static_cast<double>(v - m)); });
+  s = block_sum(s, redd);
+  const float lse = m + static_cast<float>(log(s));
+  for (int k = threadIdx.x; k < topk; k += kThreads) {
+    long long id = ids[blockIdx.x * ids_stride + k];
+    if (id < 0) id = 0;
+    if (id >= vocab) id = vocab - 1;
+    out[blockIdx.x * static_cast<long long>(topk) + k] = to_f(row[id]) - lse;
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads) ranks_kernel(int64_t* out, const T* logits, long long stride,
+                                                         const int64_t* ids, long long vocab) {
+  __shared__ long long redl[kThreads / 32];
+  const T* row = logits + blockIdx.x * stride;
+  const long long id = ids[blockIdx.x];
+  if (id < 0 || id >= vocab) {
+    if (threadIdx.x == 0) {
+      out[blockIdx.x] = 0;
+      atomicOr(&g_sampler_error, 1);
+    }
+    return;
+  }
+  const float x = to_f(row[id]);
+  long long c = 0;
+  for_row(row, vocab, [&](long long, float v) { c += v >= x ? 1 : 0; });
+  c = block_sum(c, redl);
+  if (threadIdx.x == 0) out[blockIdx.x] = c;
+}
+
+orError_t check_float(int dtype, const char* op) {
+  MCPU_ARG_CHECK(dtype == MCPU_FLOAT32 || dtype == MCPU_FLOAT16 || dtype == MCPU_BFLOAT16,
+                 "%s: logits must be float32, float16 or bfloat16 (dtype code %d)", op, dtype);
+  return orSuccess;
+}
+
+}  // namespace sampler
+
+orError_t sampler_read_error(int* flag, bool reset) {
+  MCPU_CUDA_TRY(cudaMemcpyFromSymbol(flag, sampler::g_sampler_error, sizeof(int)), "sampler error flag");
+  if (reset) {
+    const int zero = 0;
+    MCPU_CUDA_TRY(cudaMemcpyToSymbol(sampler::g_sampler_error, &zero, sizeof(int)), "sampler error flag reset");
+  }
+  return orSuccess;
+}
+
+}  // namespace mcpu
+
+using namespace mcpu;
+
+extern "C" orError_t mcpu_vllm_min_p(void* logits, int dtype, int64_t num_tokens, int64_t logits_stride,
+                                     const int32_t* expanded_idx_mapping, const float* min_p, int64_t vocab_size,
+                                     orStream_t stream) {
+  orError_t e = sampler::check_float(dtype, "vllm_min_p_kernel");
+  if (e != orSuccess) return e;
+  MCPU_ARG_CHECK(num_tokens >= 0 && num_tokens < (1LL << 31), "vllm_min_p_kernel: bad num_tokens");
+  MCPU_ARG_CHECK(vocab_size > 0 && vocab_size <= logits_stride, "vllm_min_p_kernel: vocab_size %lld out of range",
+                 static_cast<long long>(vocab_size));
+  if (num_tokens == 0) return orSuccess;
+  MCPU_ARG_CHECK(logits && expanded_idx_mapping && min_p, "vllm_min_p_kernel: NULL pointer");
+  const dim3 grid(static_cast<unsigned>(num_tokens));
+  cudaStream_t st = as_cuda(stream);
+  if (dtype == MCPU_FLOAT32)
+    sampler::min_p_kernel<float><<<grid, sampler::kThreads, 0, st>>>(static_cast<float*>(logits), logits_stride,
+                                                                       expanded_idx_mapping, min_p, vocab_size);
+  else if (dtype == MCPU_FLOAT16)
+    sampler::min_p_kernel<__half><<<grid, sampler::kThreads, 0, st>>>(static_cast<__half*>(logits), logits_stride,
+                                                                        expanded_idx_mapping, min_p, vocab_size);
+  else
+    sampler::min_p_kernel<__nv_bfloat16><<<grid, sampler::kThreads, 0, st>>>(
+        static_cast<__nv_bfloat16*>(logits), logits_stride, expanded_idx_mapping, min_p, vocab_size);
+  return from_cuda(cudaGetLastError(), "vllm_min_p_kernel launch");
+}
+
+extern "C" orError_t mcpu_vllm_topk_log_softmax(float* output, const void* logits, int dtype, int64_t batch,
+                                                int64_t logits_stride, const int64_t* topk_ids,
+                                                int64_t topk_ids_stride, int64_t topk, int64_t vocab_size,
+                                                orStream_t stream) {
+  orError_t e = sampler::check_float(dtype, "vllm_topk_log_softmax_kernel");
+  if (e != orSuccess) return e;
+  MCPU_ARG_CHECK(batch >= 0 && batch < (1LL << 31) && topk >= 0 && topk < (1LL << 31),
+                 "vllm_topk_log_softmax_kernel: bad batch or topk");
+  MCPU_ARG_CHECK(vocab_size > 0 && vocab_size <= logits_stride,
+                 "vllm_topk_log_softmax_kernel: vocab_size %lld out of range", static_cast<long long>(vocab_size));
+  if (batch == 0 || topk == 0) return orSuccess;
+  MCPU_ARG_CHECK(output && logits && topk_ids, "vllm_topk_log_softmax_kernel: NULL pointer");
+  const dim3 grid(static_cast<unsigned>(batch));
+  cudaStream_t st = as_cuda(stream);
+  if (dtype == MCPU_FLOAT32)
+    sampler::topk_log_softmax_kernel<float><<<grid, sampler::kThreads, 0, st>>>(
+        output, static_cast<const float*>(logits), logits_stride, topk_ids, topk_ids_stride, static_cast<int>(topk),
+        vocab_size);
+  else if (dtype == MCPU_FLOAT16)
+    sampler::topk_log_softmax_kernel<__half><<<grid, sampler::kThreads, 0, st>>>(
+        output, static_cast<const __half*>(logits), logits_stride, topk_ids, topk_ids_stride, static_cast<int>(topk),
+        vocab_size);
+  else
+    sampler::topk_log_softmax_kernel<__nv_bfloat16><<<grid, sampler::kThreads, 0, st>>>(
+        output, static_cast<const __nv_bfloat16*>(logits), logits_stride, topk_ids, topk_ids_stride,
+        static_cast<int>(topk), vocab_size);
+  return from_cuda(cudaGetLastError(), "vllm_topk_log_softmax_kernel launch");
+}
+
+extern "C" orError_t mcpu_vllm_ranks(int64_t* output, const void* logits, int dtype, int64_t batch,
+                                     int64_t logits_stride, const int64_t* token_ids, int64_t vocab_size,
+                                     orStream_t stream) {
+  orError_t e = sampler::check_float(dtype, "vllm_ranks_kernel");
+  if (e != orSuccess) return e;
+  MCPU_ARG_CHECK(batch >= 0 && batch < (1LL << 31), "vllm_ranks_kernel: bad batch");
+  MCPU_ARG_CHECK(vocab_size > 0 && vocab_size <= logits_stride, "vllm_ranks_kernel: vocab_size %lld out of range",
+                 static_cast<long long>(vocab_size));
+  if (batch == 0) return orSuccess;
+  MCPU_ARG_CHECK(output && logits && token_ids, "vllm_ranks_kernel: NULL pointer");
+  const dim3 grid(static_cast<unsigned>(batch));
+  cudaStream_t st = as_cuda(stream);
+  if (dtype == MCPU_FLOAT32)
+    sampler::ranks_kernel<float><<<grid, sampler::kThreads, 0, st>>>(output, static_cast<const float*>(logits),
+                                                                       logits_stride, token_ids, vocab_size);
+  else if (dtype == MCPU_FLOAT16)
+    sampler::ranks_kernel<__half><<<grid, sampler::kThreads, 0, st>>>(output, static_cast<const __half*>(logits),
+                                                                        logits_stride, token_ids, vocab_size);
+  else
+    sampler::ranks_kernel<__nv_bfloat16><<<grid, sampler::kThreads, 0, st>>>(
+        output, static_cast<const __nv_bfloat16*>(logits), logits_stride, token_ids, vocab_size);
+  return from_cuda(cudaGetLastError(), "vllm_ranks_kernel launch");
+}

@@ -636,6 +636,67 @@ void moe_align_block_size(const at::Tensor& topk_ids, int64_t num_experts, int64
           "moe_align_block_size");
 }
 
+// vLLM sampler kernels with the reference's own schemas
+// (csrc/aten/vllm_kernels/min_p.cpp:113-124, logprob.cpp:188-208).
+int sampler_dtype(const at::Tensor& t, const char* name) {
+  switch (t.scalar_type()) {
+    case at::kFloat: return MCPU_FLOAT32;
+    case at::kHalf: return MCPU_FLOAT16;
+    case at::kBFloat16: return MCPU_BFLOAT16;
+    default: TORCH_CHECK(false, name, " must be float32, float16, or bfloat16, got ", t.scalar_type());
+  }
+}
+
+void vllm_min_p_kernel(at::Tensor& logits, const at::Tensor& expanded_idx_mapping, const at::Tensor& min_p,
+                       int64_t vocab_size) {
+  TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "logits must be 2-D with unit column stride");
+  TORCH_CHECK(expanded_idx_mapping.dim() == 1 && expanded_idx_mapping.scalar_type() == at::kInt,
+              "expanded_idx_mapping must be 1-D int32");
+  TORCH_CHECK(min_p.dim() == 1 && min_p.scalar_type() == at::kFloat, "min_p must be 1-D float32");
+  TORCH_CHECK(vocab_size > 0 && vocab_size <= logits.size(1), "vocab_size ", vocab_size, " out of range [1, ",
+              logits.size(1), "]");
+  TORCH_CHECK(expanded_idx_mapping.numel() >= logits.size(0), "expanded_idx_mapping shorter than the tokens");
+  const int dt = sampler_dtype(logits, "logits");
+  const at::Tensor idx = expanded_idx_mapping.contiguous(), mp = min_p.contiguous();
+  MCPU_OK(mcpu_vllm_min_p(logits.data_ptr(), dt, logits.size(0), logits.stride(0), idx.const_data_ptr<int32_t>(),
+                          mp.const_data_ptr<float>(), vocab_size, stream_of(logits)),
+          "vllm_min_p_kernel");
+}
+
+void vllm_topk_log_softmax_kernel(at::Tensor& output, const at::Tensor& logits, const at::Tensor& topk_ids,
+                                  int64_t topk, int64_t vocab_size) {
+  TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "logits must be 2-D with unit column stride");
+  const int dt = sampler_dtype(logits, "logits");
+  TORCH_CHECK(output.dim() == 2 && output.scalar_type() == at::kFloat && output.is_contiguous(),
+              "output must be a contiguous 2-D float32 tensor");
+  TORCH_CHECK(topk_ids.dim() == 2 && topk_ids.scalar_type() == at::kLong && topk_ids.stride(1) == 1,
+              "topk_ids must be 2-D int64 with unit column stride");
+  TORCH_CHECK(vocab_size > 0 && vocab_size <= logits.size(1), "vocab_size out of range");
+  TORCH_CHECK(output.size(0) == logits.size(0) && output.size(1) == topk && topk_ids.size(1) >= topk &&
+                  topk_ids.size(0) >= logits.size(0),
+              "vllm_topk_log_softmax_kernel: shape mismatch");
+  MCPU_OK(mcpu_vllm_topk_log_softmax(output.data_ptr<float>(), logits.const_data_ptr(), dt, logits.size(0),
+                                     logits.stride(0), topk_ids.const_data_ptr<int64_t>(), topk_ids.stride(0), topk,
+                                     vocab_size, stream_of(logits)),
+          "vllm_topk_log_softmax_kernel");
+}
+
+void vllm_ranks_kernel(at::Tensor& output, const at::Tensor& logits, const at::Tensor& token_ids,
+                       int64_t vocab_size) {
+  TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "logits must be 2-D with unit column stride");
+  const int dt = sampler_dtype(logits, "logits");
+  TORCH_CHECK(output.dim() == 1 && output.scalar_type() == at::kLong && output.is_contiguous(),
+              "output must be a contiguous 1-D int64 tensor");
+  TORCH_CHECK(token_ids.dim() == 1 && token_ids.scalar_type() == at::kLong, "token_ids must be 1-D int64");
+  TORCH_CHECK(vocab_size > 0 && vocab_size <= logits.size(1), "vocab_size out of range");
+  TORCH_CHECK(output.numel() == logits.size(0) && token_ids.numel() >= logits.size(0),
+              "vllm_ranks_kernel: shape mismatch");
+  const at::Tensor ids = token_ids.contiguous();
+  MCPU_OK(mcpu_vllm_ranks(output.data_ptr<int64_t>(), logits.const_data_ptr(), dt, logits.size(0),
+                          logits.stride(0), ids.const_data_ptr<int64_t>(), vocab_size, stream_of(logits)),
+          "vllm_ranks_kernel");
+}
+
 // Row-parallel down projection + SUM all-reduce of the partials in one kernel
 // (mm, csrc/aten/ops/mm.cpp:13-51, then McpuBackend::allreduce,
 // torch_mcpu/csrc/Distributed.cpp:403-413).  `window` is the address of the
@@ -735,6 +796,10 @@ TORCH_LIBRARY_FRAGMENT(mcpu, m) {
   m.def("gemm_swiglu(Tensor x, Tensor w_gate_up_interleaved) -> Tensor");
   m.def("gemm_swiglu.out(Tensor x, Tensor w_gate_up_interleaved, *, Tensor(a!) out) -> Tensor(a!)");
   m.def("mm_allreduce(Tensor a, Tensor b, int window) -> Tensor");
+  m.def("vllm_min_p_kernel(Tensor(a!) logits, Tensor expanded_idx_mapping, Tensor min_p, int vocab_size) -> ()");
+  m.def("vllm_topk_log_softmax_kernel(Tensor(a!) output, Tensor logits, Tensor topk_ids, int topk, "
+        "int vocab_size) -> ()");
+  m.def("vllm_ranks_kernel(Tensor(a!) output, Tensor logits, Tensor token_ids, int vocab_size) -> ()");
   m.def("moe_align_block_size(Tensor topk_ids, int num_experts, int block_size, Tensor(a!) sorted_token_ids, "
         "Tensor(b!) experts_ids, Tensor(c!) num_tokens_post_pad) -> ()");
 }
@@ -747,5 +812,8 @@ TORCH_LIBRARY_IMPL(mcpu, PrivateUse1, m) {
   m.impl("gemm_swiglu", gemm_swiglu);
   m.impl("gemm_swiglu.out", gemm_swiglu_out);
   m.impl("mm_allreduce", mm_allreduce);
+  m.impl("vllm_min_p_kernel", vllm_min_p_kernel);
+  m.impl("vllm_topk_log_softmax_kernel", vllm_topk_log_softmax_kernel);
+  m.impl("vllm_ranks_kernel", vllm_ranks_kernel);
   m.impl("moe_align_block_size", moe_align_block_size);
 }
