@@ -7,10 +7,14 @@
 //                                 (logprob.cpp:15-69)
 //   vllm_ranks_kernel             number of logits >= the sampled token's
 //                                 (logprob.cpp:123-149)
-// One 1024-thread CTA per row: a pass for the row maximum (16-byte loads
-// where the row allows), then the op's pass over the row again (from L2).
-// Logits are fp32, fp16 or bf16, compared as fp32 like the reference; the
-// log-sum-exp accumulates exp(x - max) in fp64 as the reference does.
+// Each row is split over a cluster of 8 CTAs (256 threads each): every CTA
+// streams its eighth of the row (16-byte loads, four in flight per thread,
+// where the row start allows), the CTAs combine their partial maxima, sums
+// or counts through distributed shared memory in rank order, and each then
+// runs the op's pass over its eighth again (from L2).  Logits are fp32,
+// fp16 or bf16, compared as fp32 like the reference; the log-sum-exp sums
+// exp(x - max) in fp64 as the reference does, each term from the fp32 exp.
+#include <cooperative_groups.h>
 #include <math.h>
 
 #include "common.cuh"
@@ -18,7 +22,10 @@
 namespace mcpu {
 namespace sampler {
 
-constexpr int kThreads = 1024;
+namespace cg = cooperative_groups;
+
+constexpr int kThreads = 256;  // per CTA
+constexpr int kCluster = 8;    // CTAs per row
 
 __device__ int g_sampler_error = 0;
 
@@ -40,17 +47,19 @@ __device__ __forceinline__ __half neg_inf<__half>() { return __ushort_as_half(0x
 template <>
 __device__ __forceinline__ __nv_bfloat16 neg_inf<__nv_bfloat16>() { return __ushort_as_bfloat16(0xFF80); }
 
-// Calls f(i, value) for every element of the row: 16-byte vectors when the
-// row start is 16-byte aligned, scalars for the rest.
+// Calls f(i, value) for every element of this CTA's part of the row: with a
+// 16-byte-aligned row start, the row's 16-byte vectors are split evenly over
+// the cluster (the last CTA also takes the scalar tail); otherwise the
+// elements are.
 template <typename T, typename F>
-__device__ __forceinline__ void for_row(const T* row, long long n, F&& f) {
+__device__ __forceinline__ void for_part(const T* row, long long n, int part, F&& f) {
   constexpr int V = 16 / sizeof(T);
-  long long head = 0;
   if ((reinterpret_cast<uintptr_t>(row) & 15) == 0) {
     const long long nv = n / V;
+    const long long v0 = nv * part / kCluster, v1 = nv * (part + 1) / kCluster;
     const uint4* rv = reinterpret_cast<const uint4*>(row);
-    long long j = threadIdx.x;
-    for (; j + 3 * kThreads < nv; j += 4 * kThreads) {  // four 16-byte loads in flight per thread
+    long long j = v0 + threadIdx.x;
+    for (; j + 3 * kThreads < v1; j += 4 * kThreads) {  // four 16-byte loads in flight per thread
       uint4 u[4];
 #pragma unroll
       for (int r = 0; r < 4; ++r) u[r] = __ldg(rv + j + r * kThreads);
@@ -61,15 +70,18 @@ __device__ __forceinline__ void for_row(const T* row, long long n, F&& f) {
         for (int k = 0; k < V; ++k) f((j + r * kThreads) * V + k, to_f(t[k]));
       }
     }
-    for (; j < nv; j += kThreads) {
+    for (; j < v1; j += kThreads) {
       const uint4 u = __ldg(rv + j);
       const T* t = reinterpret_cast<const T*>(&u);
 #pragma unroll
       for (int k = 0; k < V; ++k) f(j * V + k, to_f(t[k]));
     }
-    head = nv * V;
+    if (part == kCluster - 1)
+      for (long long i = nv * V + threadIdx.x; i < n; i += kThreads) f(i, to_f(row[i]));
+  } else {
+    const long long e0 = n * part / kCluster, e1 = n * (part + 1) / kCluster;
+    for (long long i = e0 + threadIdx.x; i < e1; i += kThreads) f(i, to_f(row[i]));
   }
-  for (long long i = head + threadIdx.x; i < n; i += kThreads) f(i, to_f(row[i]));
 }
 
 __device__ __forceinline__ float block_max(float v, float* red) {
@@ -99,67 +111,123 @@ __device__ __forceinline__ A block_sum(A v, A* red) {
   return v;
 }
 
+// Combines one value per CTA of the cluster, in rank order, on every CTA.
+// `slot` is this CTA's shared variable holding its value.
+template <typename A, typename Op>
+__device__ __forceinline__ A cluster_combine(A* slot, A init, Op op) {
+  cg::cluster_group cluster = cg::this_cluster();
+  cluster.sync();  // every CTA's slot is written
+  A v = init;
+#pragma unroll
+  for (int r = 0; r < kCluster; ++r) v = op(v, *cluster.map_shared_rank(slot, r));
+  cluster.sync();  // every CTA has read every slot before any reuses or leaves
+  return v;
+}
+
 // The row maximum as the reference takes it: a running `v > max` from -inf,
 // so NaN never becomes the maximum.
 template <typename T>
-__device__ __forceinline__ float row_max(const T* row, long long n, float* red) {
+__device__ __forceinline__ float row_max(const T* row, long long n, int part, float* red, float* slot) {
   float m = -INFINITY;
-  for_row(row, n, [&](long long, float v) { m = v > m ? v : m; });
-  return block_max(m, red);
+  for_part(row, n, part, [&](long long, float v) { m = v > m ? v : m; });
+  m = block_max(m, red);
+  if (threadIdx.x == 0) *slot = m;
+  return cluster_combine(slot, -INFINITY, [](float a, float b) { return fmaxf(a, b); });
 }
 
 template <typename T>
-__global__ void __launch_bounds__(kThreads) min_p_kernel(T* logits, long long stride, const int32_t* idx,
-                                                         const float* min_p, long long vocab) {
+__global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
+    min_p_kernel(T* logits, long long stride, const int32_t* idx, const float* min_p, long long vocab) {
   __shared__ float red[kThreads / 32];
-  T* row = logits + blockIdx.x * stride;
-  const float mp = min_p[idx[blockIdx.x]];
-  if (mp == 0.0f) return;
+  __shared__ float slot;
+  const long long r = blockIdx.x / kCluster;
+  const int part = blockIdx.x % kCluster;
+  T* row = logits + r * stride;
+  const float mp = min_p[idx[r]];
+  if (mp == 0.0f) return;  // the same for every CTA of the cluster
   // log(p) rounded once from fp64: the fp32 logarithm to within rounding
-  const float thr = row_max(row, vocab, red) + static_cast<float>(log(static_cast<double>(mp)));
-  for_row(static_cast<const T*>(row), vocab, [&](long long i, float v) {
-    if (v < thr) row[i] = neg_inf<T>();
-  });
-}
-
-template <typename T>
-__global__ void __launch_bounds__(kThreads) topk_log_softmax_kernel(float* out, const T* logits, long long stride,
-                                                                    const int64_t* ids, long long ids_stride,
-                                                                    int topk, long long vocab) {
-  __shared__ float red[kThreads / 32];
-  __shared__ double redd[kThreads / 32];
-  const T* row = logits + blockIdx.x * stride;
-  const float m = row_max(row, vocab, red);
-  double s = 0.0;
-  for_row(row, vocab, [&](long long, float v) { s += exp(static_cast<double>(v - m)); });
-  s = block_sum(s, redd);
-  const float lse = m + static_cast<float>(log(s));
-  for (int k = threadIdx.x; k < topk; k += kThreads) {
-    long long id = ids[blockIdx.x * ids_stride + k];
-    if (id < 0) id = 0;
-    if (id >= vocab) id = vocab - 1;
-    out[blockIdx.x * static_cast<long long>(topk) + k] = to_f(row[id]) - lse;
+  const float thr = row_max(row, vocab, part, red, &slot) + static_cast<float>(log(static_cast<double>(mp)));
+  // the compare pass, one 16-byte store per vector that changes
+  constexpr int V = 16 / sizeof(T);
+  if ((reinterpret_cast<uintptr_t>(row) & 15) == 0) {
+    const long long nv = vocab / V;
+    const long long v0 = nv * part / kCluster, v1 = nv * (part + 1) / kCluster;
+    uint4* rv = reinterpret_cast<uint4*>(row);
+    for (long long j = v0 + threadIdx.x; j < v1; j += kThreads) {
+      uint4 u = __ldg(rv + j);
+      T* t = reinterpret_cast<T*>(&u);
+      bool any = false;
+#pragma unroll
+      for (int k = 0; k < V; ++k) {
+        if (to_f(t[k]) < thr) {
+          t[k] = neg_inf<T>();
+          any = true;
+        }
+      }
+      if (any) rv[j] = u;
+    }
+    if (part == kCluster - 1)
+      for (long long i = nv * V + threadIdx.x; i < vocab; i += kThreads)
+        if (to_f(row[i]) < thr) row[i] = neg_inf<T>();
+  } else {
+    for_part(static_cast<const T*>(row), vocab, part, [&](long long i, float v) {
+      if (v < thr) row[i] = neg_inf<T>();
+    });
   }
 }
 
 template <typename T>
-__global__ void __launch_bounds__(kThreads) ranks_kernel(int64_t* out, const T* logits, long long stride,
-                                                         const int64_t* ids, long long vocab) {
+__global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
+    topk_log_softmax_kernel(float* out, const T* logits, long long stride, const int64_t* ids, long long ids_stride,
+                            int topk, long long vocab) {
+  __shared__ float red[kThreads / 32];
+  __shared__ double redd[kThreads / 32];
+  __shared__ float slot;
+  __shared__ double dslot;
+  const long long r = blockIdx.x / kCluster;
+  const int part = blockIdx.x % kCluster;
+  const T* row = logits + r * stride;
+  const float m = row_max(row, vocab, part, red, &slot);
+  double s = 0.0;
+  // exp in fp32 (within about one ulp of the fp64 exp the reference takes),
+  // summed in fp64 like the reference
+  for_part(row, vocab, part, [&](long long, float v) { s += static_cast<double>(expf(v - m)); });
+  s = block_sum(s, redd);
+  if (threadIdx.x == 0) dslot = s;
+  s = cluster_combine(&dslot, 0.0, [](double a, double b) { return a + b; });
+  if (part != 0) return;
+  const float lse = m + static_cast<float>(log(s));
+  for (int k = threadIdx.x; k < topk; k += kThreads) {
+    long long id = ids[r * ids_stride + k];
+    if (id < 0) id = 0;
+    if (id >= vocab) id = vocab - 1;
+    out[r * static_cast<long long>(topk) + k] = to_f(row[id]) - lse;
+  }
+}
+
+template <typename T>
+__global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
+    ranks_kernel(int64_t* out, const T* logits, long long stride, const int64_t* ids, long long vocab) {
   __shared__ long long redl[kThreads / 32];
-  const T* row = logits + blockIdx.x * stride;
-  const long long id = ids[blockIdx.x];
-  if (id < 0 || id >= vocab) {
-    if (threadIdx.x == 0) {
-      out[blockIdx.x] = 0;
+  __shared__ long long slot;
+  const long long r = blockIdx.x / kCluster;
+  const int part = blockIdx.x % kCluster;
+  const T* row = logits + r * stride;
+  const long long id = ids[r];
+  if (id < 0 || id >= vocab) {  // the same for every CTA of the cluster
+    if (part == 0 && threadIdx.x == 0) {
+      out[r] = 0;
       atomicOr(&g_sampler_error, 1);
     }
     return;
   }
   const float x = to_f(row[id]);
   long long c = 0;
-  for_row(row, vocab, [&](long long, float v) { c += v >= x ? 1 : 0; });
+  for_part(row, vocab, part, [&](long long, float v) { c += v >= x ? 1 : 0; });
   c = block_sum(c, redl);
-  if (threadIdx.x == 0) out[blockIdx.x] = c;
+  if (threadIdx.x == 0) slot = c;
+  c = cluster_combine(&slot, 0LL, [](long long a, long long b) { return a + b; });
+  if (part == 0 && threadIdx.x == 0) out[r] = c;
 }
 
 orError_t check_float(int dtype, const char* op) {
@@ -193,7 +261,8 @@ extern "C" orError_t mcpu_vllm_min_p(void* logits, int dtype, int64_t num_tokens
                  static_cast<long long>(vocab_size));
   if (num_tokens == 0) return orSuccess;
   MCPU_ARG_CHECK(logits && expanded_idx_mapping && min_p, "vllm_min_p_kernel: NULL pointer");
-  const dim3 grid(static_cast<unsigned>(num_tokens));
+  MCPU_ARG_CHECK(num_tokens <= (1LL << 31) / sampler::kCluster - 1, "vllm_min_p_kernel: too many rows");
+  const dim3 grid(static_cast<unsigned>(num_tokens * sampler::kCluster));
   cudaStream_t st = as_cuda(stream);
   if (dtype == MCPU_FLOAT32)
     sampler::min_p_kernel<float><<<grid, sampler::kThreads, 0, st>>>(static_cast<float*>(logits), logits_stride,
@@ -219,7 +288,8 @@ extern "C" orError_t mcpu_vllm_topk_log_softmax(float* output, const void* logit
                  "vllm_topk_log_softmax_kernel: vocab_size %lld out of range", static_cast<long long>(vocab_size));
   if (batch == 0 || topk == 0) return orSuccess;
   MCPU_ARG_CHECK(output && logits && topk_ids, "vllm_topk_log_softmax_kernel: NULL pointer");
-  const dim3 grid(static_cast<unsigned>(batch));
+  MCPU_ARG_CHECK(batch <= (1LL << 31) / sampler::kCluster - 1, "vllm_topk_log_softmax_kernel: too many rows");
+  const dim3 grid(static_cast<unsigned>(batch * sampler::kCluster));
   cudaStream_t st = as_cuda(stream);
   if (dtype == MCPU_FLOAT32)
     sampler::topk_log_softmax_kernel<float><<<grid, sampler::kThreads, 0, st>>>(
@@ -246,7 +316,8 @@ extern "C" orError_t mcpu_vllm_ranks(int64_t* output, const void* logits, int dt
                  static_cast<long long>(vocab_size));
   if (batch == 0) return orSuccess;
   MCPU_ARG_CHECK(output && logits && token_ids, "vllm_ranks_kernel: NULL pointer");
-  const dim3 grid(static_cast<unsigned>(batch));
+  MCPU_ARG_CHECK(batch <= (1LL << 31) / sampler::kCluster - 1, "vllm_ranks_kernel: too many rows");
+  const dim3 grid(static_cast<unsigned>(batch * sampler::kCluster));
   cudaStream_t st = as_cuda(stream);
   if (dtype == MCPU_FLOAT32)
     sampler::ranks_kernel<float><<<grid, sampler::kThreads, 0, st>>>(output, static_cast<const float*>(logits),
