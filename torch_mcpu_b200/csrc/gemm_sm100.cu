@@ -27,14 +27,16 @@
 // over NVLink (mcpu_mm_allreduce):
 //   phase A  each epilogue warp converts its 32 accumulator rows to bf16 and
 //            writes them, staged through shared memory as full 128-byte
-//            lines, into the window of the slice's owner rank; then it
-//            bumps the owner's four unit counters (release, system scope);
+//            lines, into the window of the slice's owner rank; then, after
+//            a warp barrier, it bumps the owner's four unit counters
+//            (release, system scope: cumulative over the warp's stores);
 //   phase B  four more warps per CTA (warps 6-9), running beside the GEMM
 //            from the start, take this rank's units (8 rows x 256 columns
 //            of a slice) in tile order: wait until all ranks' partials have
 //            arrived, sum them in fp32 in rank order, round once to bf16
-//            and store the rows into every rank's output; at the end, one
-//            fence and one increment of every rank's done counter;
+//            and store the rows into every rank's output; at the end, a
+//            warp barrier and one release increment of every rank's done
+//            counter;
 //   finish   one thread waits for its own done counter to reach the number
 //            of units, so the launch ends only when this rank's output is
 //            complete.
@@ -239,7 +241,8 @@ __device__ __forceinline__ void ar_reducer(const Params& p, int rslot, int nr, i
     ++processed;
   }
   if (processed) {
-    peer::fence_sys();
+    // the warp barrier orders every lane's stores before the signalling
+    // lanes' release (release is cumulative): no per-lane system fence
     __syncwarp();
     if (lane < world) peer::red_add_release_sys(reinterpret_cast<uint32_t*>(p.ar.base[lane]), processed);
   }
@@ -422,7 +425,8 @@ __global__ void __launch_bounds__(kAR ? THREADS_AR : THREADS, 1)
         }
         tc_fence_before();
         mbar_arrive(&s->tmem_empty[acc]);
-        peer::fence_sys();
+        // every lane's stores are ordered before the signalling lanes'
+        // release by the warp barrier (release is cumulative)
         __syncwarp();
         if (lane < kUnitsPerSlice)
           peer::red_add_release_sys(
