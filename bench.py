@@ -428,7 +428,8 @@ def moe_leg(dev, ids, stream, reps=8, per_graph=32):
 def sampler_leg(dev, reps=20):
     """The reference's vLLM sampler ops on a decode batch: 256 rows x 128256
     vocab fp32 logits (131 MB, more than L2): min_p in place (p = 0.05 on
-    every row) and top-5 log-probabilities; CUDA-event time per call and
+    every row), top-5 log-probabilities and the repetition / frequency /
+    presence penalties in place; CUDA-event time per call and
     GB/s of the algorithmic bytes (the logits read once; each row's second
     pass re-reads it from L2)."""
     import torch
@@ -453,6 +454,21 @@ def sampler_leg(dev, reps=20):
          lambda i: _lib.check(lib.mcpu_vllm_topk_log_softmax(out.data_ptr(), xs[i % 2].data_ptr(), 0, rows, vocab,
                                                              ids.data_ptr(), 5, 5, vocab, s), "log_softmax")),
     ]
+    # penalties: every row its own request, repetition 1.1, frequency and
+    # presence 0.1, prompt bits and output counts random; bytes = the logits
+    # read and written, the counts and the bit mask read once
+    cols = (vocab + 31) // 32
+    rep = torch.full((rows,), 1.1, dtype=torch.float32, device=dev)
+    fp = torch.full((rows,), 0.1, dtype=torch.float32, device=dev)
+    pbm = torch.randint(-2 ** 31, 2 ** 31 - 1, (rows, cols), dtype=torch.int32, device=dev, generator=g)
+    obc = torch.randint(0, 3, (rows, vocab), dtype=torch.int32, device=dev, generator=g)
+    zeros = torch.zeros(rows, dtype=torch.int32, device=dev)
+    cases.append(
+        ("vllm_penalties", rows * vocab * 12 + rows * cols * 4,
+         lambda i: _lib.check(lib.mcpu_vllm_penalties(xs[i % 2].data_ptr(), 0, rows, vocab, idx.data_ptr(),
+                                                      zeros.data_ptr(), zeros.data_ptr(), rep.data_ptr(),
+                                                      fp.data_ptr(), fp.data_ptr(), rows, pbm.data_ptr(), cols,
+                                                      obc.data_ptr(), vocab, vocab, 0, s), "penalties")))
     res = {}
     for name, nbytes, fn in cases:
         for i in range(3):

@@ -289,6 +289,42 @@ OPENREG_EXPORT orError_t mcpu_vllm_ranks(int64_t* output, const void* logits, in
                                          int64_t logits_stride, const int64_t* token_ids, int64_t vocab_size,
                                          orStream_t stream);
 
+/*
+ * Penalties (penalties.cpp:14-84, mcpu::vllm_penalties_kernel): for token
+ *   row t of logits, request q = expanded_idx_mapping[t] (rep, freq, pres =
+ *   the three penalty arrays [max_num_reqs] at q; rows with 1, 0, 0 are left
+ *   as they are), count[v] = output_bin_counts[q, v] plus, when
+ *   expanded_local_pos[t] = pos > 0 and max_spec_len > 0, the number of
+ *   token_ids[t-pos+1 .. t] equal to v.  Where rep != 1 and v is in the prompt
+ *   (bit v of prompt_bin_mask row q, int32 words) or count > 0, l = l / rep
+ *   for l > 0 else l * rep; then l -= freq * count and l -= pres * [count > 0],
+ *   each operation rounded to fp32, the result to the logits dtype, in place.
+ *   A request index out of range, or pos > t, leaves the row and sets
+ *   mcpu_device_error (the reference reads out of bounds).
+ * Bincount (penalties.cpp:187-246, mcpu::vllm_bincount_kernel): for each of
+ *   the num_reqs requests q = expanded_idx_mapping[i], sets bit tok of
+ *   prompt_bin_mask row q for the all_token_ids[q, 0 .. prompt_len[q]) and
+ *   adds 1 to output_bin_counts[q, tok] for all_token_ids[q, prompt_len[q] ..
+ *   prefill_len[q]); tokens outside [0, vocab) are skipped; the outputs are
+ *   accumulated into (zero them first).  A request index out of range, or
+ *   lengths outside [0, max_seq_len], set mcpu_device_error.
+ */
+OPENREG_EXPORT orError_t mcpu_vllm_penalties(void* logits, int dtype, int64_t num_tokens, int64_t logits_stride,
+                                             const int32_t* expanded_idx_mapping, const int32_t* token_ids,
+                                             const int32_t* expanded_local_pos, const float* repetition_penalty,
+                                             const float* frequency_penalty, const float* presence_penalty,
+                                             int64_t max_num_reqs, const int32_t* prompt_bin_mask,
+                                             int64_t pbm_stride, const int32_t* output_bin_counts,
+                                             int64_t obc_stride, int64_t vocab_size, int64_t max_spec_len,
+                                             orStream_t stream);
+OPENREG_EXPORT orError_t mcpu_vllm_bincount(const int32_t* expanded_idx_mapping, int64_t num_reqs,
+                                            const int32_t* all_token_ids, int64_t tids_stride,
+                                            int64_t max_seq_len, const int32_t* prompt_len,
+                                            const int32_t* prefill_len, int64_t max_num_reqs,
+                                            int32_t* prompt_bin_mask, int64_t packed_cols, int64_t pbm_stride,
+                                            int32_t* output_bin_counts, int64_t vocab_size, int64_t obc_stride,
+                                            orStream_t stream);
+
 /* *flag = 1 if a kernel on the current device (tensor-core GEMM, TMA-fed
  * router or bulk-copy-fed rms_norm) gave up on a bounded wait, or a gather /
  * scatter met an index out of range, since the last reset; that launch left

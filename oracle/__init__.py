@@ -277,3 +277,59 @@ def vllm_ranks(logits: np.ndarray, token_ids: np.ndarray, vocab: int) -> np.ndar
     lg = np.asarray(logits, dtype=np.float32)
     return np.array([int((lg[r, :vocab] >= lg[r, int(token_ids[r])]).sum()) for r in range(lg.shape[0])],
                     dtype=np.int64)
+
+
+def vllm_penalties(logits: np.ndarray, idx: np.ndarray, token_ids: np.ndarray, local_pos: np.ndarray,
+                   rep: np.ndarray, freq: np.ndarray, pres: np.ndarray, prompt_bin_mask: np.ndarray,
+                   output_bin_counts: np.ndarray, vocab: int, max_spec_len: int) -> np.ndarray:
+    """penalties.cpp:14-84: repetition / frequency / presence penalties of
+    each token row, returned as new fp32 logits.  count[v] = output count of
+    the row's request plus the row's draft tokens token_ids[t-pos+1 .. t]
+    equal to v (pos = local_pos[t] > 0 and max_spec_len > 0); where rep != 1
+    and v is in the prompt bit mask or count > 0: l / rep for l > 0, else
+    l * rep; then l - freq * count, l - pres * [count > 0], each an fp32
+    operation."""
+    lg = np.array(logits, dtype=np.float32, copy=True)
+    v = np.arange(vocab)
+    for t in range(lg.shape[0]):
+        q = int(idx[t])
+        rp, fp, pp = np.float32(rep[q]), np.float32(freq[q]), np.float32(pres[q])
+        if rp == 1 and fp == 0 and pp == 0:
+            continue
+        cnt = np.array(output_bin_counts[q, :vocab], dtype=np.int64)
+        pos = int(local_pos[t])
+        if pos > 0 and max_spec_len > 0:
+            for prev in range(pos):
+                d = int(token_ids[t - pos + prev + 1])
+                if 0 <= d < vocab:
+                    cnt[d] += 1
+        out = cnt > 0
+        x = lg[t, :vocab].copy()
+        if rp != 1:
+            words = np.asarray(prompt_bin_mask[q], dtype=np.int32).view(np.uint32)[v >> 5]
+            hit = ((words >> (v & 31).astype(np.uint32)) & 1).astype(bool) | out
+            x = np.where(hit, np.where(x > 0, x / rp, x * rp), x).astype(np.float32)
+        x = (x - fp * cnt.astype(np.float32)).astype(np.float32)
+        x = (x - pp * out.astype(np.float32)).astype(np.float32)
+        lg[t, :vocab] = x
+    return lg
+
+
+def vllm_bincount(idx: np.ndarray, all_token_ids: np.ndarray, prompt_len: np.ndarray, prefill_len: np.ndarray,
+                  prompt_bin_mask: np.ndarray, output_bin_counts: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+    """penalties.cpp:187-246: for each listed request q, bit tok of the prompt
+    mask row q for the first prompt_len[q] tokens, +1 in the output counts
+    row q for tokens prompt_len[q] .. prefill_len[q]; tokens outside the mask
+    or the vocabulary are skipped.  Accumulates into copies of the inputs."""
+    pbm = np.array(prompt_bin_mask, dtype=np.int32, copy=True)
+    obc = np.array(output_bin_counts, dtype=np.int32, copy=True)
+    pu = pbm.view(np.uint32)
+    cols, vocab = pbm.shape[1], obc.shape[1]
+    for q in np.asarray(idx, dtype=np.int64):
+        p, f = int(prompt_len[q]), int(prefill_len[q])
+        pt = np.asarray(all_token_ids[q, :p], dtype=np.int64)
+        pt = pt[(pt >= 0) & (pt // 32 < cols)]
+        np.bitwise_or.at(pu[q], pt // 32, (np.uint32(1) << (pt % 32).astype(np.uint32)))
+        ot = np.asarray(all_token_ids[q, p:f], dtype=np.int64)
+        np.add.at(obc[q], ot[(ot >= 0) & (ot < vocab)], 1)
+    return pbm, obc

@@ -1,12 +1,14 @@
 """The reference's vLLM sampler ops (mcpu::vllm_min_p_kernel,
 vllm_topk_log_softmax_kernel, vllm_ranks_kernel; csrc/aten/vllm_kernels/
-min_p.cpp, logprob.cpp) on the B200 against the oracle, called as the
+min_p.cpp, logprob.cpp; vllm_penalties_kernel, vllm_bincount_kernel:
+penalties.cpp) on the B200 against the oracle, called as the
 reference's users call them (torch.ops.mcpu on mcpu tensors): fp32, fp16
 and bf16 logits, vocabularies with 16-byte-aligned and unaligned rows, a
 row stride wider than the vocabulary, -inf and NaN entries, p = 0 rows and
 out-of-range ids.  ranks are exact; log-probabilities within 2e-6; min_p
 results identical except where an entry lies within one fp32 ulp of the
-threshold (the threshold's logarithm is rounded once from fp64)."""
+threshold (the threshold's logarithm is rounded once from fp64); penalties
+and bincount bit-exact."""
 
 import numpy as np
 import pytest
@@ -84,3 +86,76 @@ def test_argument_errors(mcpu):
         torch.ops.mcpu.vllm_ranks_kernel(torch.zeros(2, dtype=torch.int64, device="mcpu"),
                                          torch.zeros(2, 8, dtype=torch.int32, device="mcpu"),
                                          torch.zeros(2, dtype=torch.int64, device="mcpu"), 8)
+
+
+def _penalty_batch(vocab, seed):
+    """Six requests with prompts and generated tokens (some outside the
+    vocabulary), bit masks and counts built by the bincount op, and ten token
+    rows of speculative decoding: request r owns rows at local positions
+    0 .. k_r - 1."""
+    g = torch.Generator().manual_seed(seed)
+    reqs, seq = 6, 700
+    tids = torch.randint(-2, vocab + 3, (reqs, seq), generator=g, dtype=torch.int32)
+    plen = torch.randint(0, 400, (reqs,), generator=g, dtype=torch.int32)
+    flen = plen + torch.randint(0, 300, (reqs,), generator=g, dtype=torch.int32)
+    rep = torch.tensor([1.0, 1.3, 0.8, 1.0, 2.0, 1.1], dtype=torch.float32)
+    freq = torch.tensor([0.0, 0.2, 0.0, 0.5, -0.3, 0.05], dtype=torch.float32)
+    pres = torch.tensor([0.0, 0.1, 0.7, 0.0, 0.25, -0.4], dtype=torch.float32)
+    rows_of = [1, 3, 2, 1, 2, 1]
+    idx = torch.tensor([r for r, k in enumerate(rows_of) for _ in range(k)], dtype=torch.int32)
+    lpos = torch.tensor([p for k in rows_of for p in range(k)], dtype=torch.int32)
+    drafts = torch.randint(0, vocab, (idx.numel(),), generator=g, dtype=torch.int32)
+    drafts[2] = int(tids[1, plen[1]]) if flen[1] > plen[1] else 5  # a draft also in the output
+    return dict(tids=tids, plen=plen, flen=flen, rep=rep, freq=freq, pres=pres, idx=idx, lpos=lpos,
+                drafts=drafts, reqs=reqs)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("width,vocab", [(32000, 32000), (151937, 151937), (50016, 50000)])
+def test_bincount_and_penalties(mcpu, dtype, width, vocab):
+    b = _penalty_batch(vocab, 4)
+    cols = (vocab + 31) // 32
+    pbm0 = torch.zeros(b["reqs"], cols, dtype=torch.int32)
+    obc0 = torch.zeros(b["reqs"], vocab, dtype=torch.int32)
+    pbm, obc = pbm0.to("mcpu"), obc0.to("mcpu")
+    listed = torch.tensor([0, 1, 2, 3, 4, 5], dtype=torch.int32)
+    torch.ops.mcpu.vllm_bincount_kernel(listed.to("mcpu"), b["tids"].to("mcpu"), b["plen"].to("mcpu"),
+                                        b["flen"].to("mcpu"), pbm, obc)
+    wp, wo = oracle.vllm_bincount(listed.numpy(), b["tids"].numpy(), b["plen"].numpy(), b["flen"].numpy(),
+                                  pbm0.numpy(), obc0.numpy())
+    np.testing.assert_array_equal(pbm.cpu().numpy(), wp)
+    np.testing.assert_array_equal(obc.cpu().numpy(), wo)
+
+    rows = b["idx"].numel()
+    x = _logits(rows, width, dtype, 5)
+    x[1, 7] = 1.5  # no NaN: the reference's NaN conversion to 16-bit types is not CUDA's
+    for max_spec in (0, 3):
+        xm = x.to("mcpu")
+        torch.ops.mcpu.vllm_penalties_kernel(xm, b["idx"].to("mcpu"), b["drafts"].to("mcpu"),
+                                             b["lpos"].to("mcpu"), b["rep"].to("mcpu"), b["freq"].to("mcpu"),
+                                             b["pres"].to("mcpu"), pbm, obc, vocab, max_spec)
+        want = oracle.vllm_penalties(x.float().numpy(), b["idx"].numpy(), b["drafts"].numpy(), b["lpos"].numpy(),
+                                     b["rep"].numpy(), b["freq"].numpy(), b["pres"].numpy(), wp, wo, vocab,
+                                     max_spec)
+        want = torch.from_numpy(want).to(dtype)
+        got = xm.cpu()
+        assert torch.equal(got.view(torch.int16 if dtype != torch.float32 else torch.int32),
+                           want.view(torch.int16 if dtype != torch.float32 else torch.int32)), max_spec
+        assert not torch.equal(got, x)  # the penalties changed something
+
+
+def test_penalties_bad_request_index(mcpu):
+    from torch_mcpu_b200.ops import device_error
+
+    device_error(reset=True)
+    x = torch.ones(2, 64, device="mcpu")
+    one = torch.ones(1, device="mcpu")
+    torch.ops.mcpu.vllm_penalties_kernel(x, torch.tensor([0, 7], dtype=torch.int32, device="mcpu"),
+                                         torch.zeros(2, dtype=torch.int32, device="mcpu"),
+                                         torch.zeros(2, dtype=torch.int32, device="mcpu"), 2 * one, one, one,
+                                         torch.full((1, 2), -1, dtype=torch.int32, device="mcpu"),
+                                         torch.zeros(1, 64, dtype=torch.int32, device="mcpu"), 64, 0)
+    got = x.cpu()
+    assert torch.equal(got[1], torch.ones(64))  # request 7 of 1: the row is left, the flag set
+    assert torch.equal(got[0], torch.full((64,), 0.5))  # all in the prompt: 1 / 2
+    assert device_error(reset=True) == 1

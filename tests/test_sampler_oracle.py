@@ -24,3 +24,48 @@ def test_log_softmax_and_ranks_known_answers():
     np.testing.assert_allclose(lp[0], np.log([0.5, 1 / 6, 1 / 6, 1 / 6]), rtol=1e-6)  # 99 and -5 clamp
     assert oracle.vllm_ranks(x, np.array([1]), 4).tolist() == [1]
     assert oracle.vllm_ranks(x, np.array([0]), 4).tolist() == [4]  # ties count
+
+
+def test_penalties_known_answers():
+    """penalties.cpp:14-84 by hand: vocab 4, rep 2, freq 0.5, pres 0.25; token 0
+    in the prompt, token 2 generated three times."""
+    lg = np.array([[2.0, -2.0, 1.0, 4.0]], dtype=np.float32)
+    pbm = np.array([[0b0001]], dtype=np.int32)
+    obc = np.array([[0, 0, 3, 0]], dtype=np.int32)
+    out = oracle.vllm_penalties(lg, np.array([0]), np.array([1]), np.array([0]), np.array([2.0]),
+                                np.array([0.5]), np.array([0.25]), pbm, obc, 4, 0)
+    # 2 / 2 = 1; -2 untouched; 1 / 2 - 0.5 * 3 - 0.25 = -1.25; 4 untouched
+    assert out.tolist() == [[1.0, -2.0, -1.25, 4.0]]
+    # a negative logit in the prompt is multiplied: -2 * 2
+    out = oracle.vllm_penalties(lg, np.array([0]), np.array([1]), np.array([0]), np.array([2.0]),
+                                np.array([0.0]), np.array([0.0]), np.array([[0b0010]], dtype=np.int32),
+                                np.zeros((1, 4), np.int32), 4, 0)
+    assert out.tolist() == [[2.0, -4.0, 1.0, 4.0]]
+    # neutral penalties leave the row, whatever the counts
+    out = oracle.vllm_penalties(lg, np.array([0]), np.array([1]), np.array([0]), np.array([1.0]),
+                                np.array([0.0]), np.array([0.0]), pbm, obc, 4, 0)
+    assert np.array_equal(out, lg)
+
+
+def test_penalties_draft_tokens():
+    """Row t at local position pos counts the drafts token_ids[t-pos+1 .. t],
+    and only with max_spec_len > 0."""
+    lg = np.ones((3, 4), dtype=np.float32)
+    args = (np.array([0, 0, 0]), np.array([9, 3, 2]), np.array([0, 1, 2]), np.array([1.0]), np.array([1.0]),
+            np.array([0.0]), np.zeros((1, 1), np.int32), np.zeros((1, 4), np.int32), 4)
+    out = oracle.vllm_penalties(lg, *args, 2)
+    assert out.tolist() == [[1, 1, 1, 1], [1, 1, 1, 0], [1, 1, 0, 0]]
+    assert np.array_equal(oracle.vllm_penalties(lg, *args, 0), lg)
+
+
+def test_bincount_known_answers():
+    tids = np.array([[0, 0, 0, 0], [33, 1, 1, 5]])
+    pbm, obc = oracle.vllm_bincount(np.array([1]), tids, np.array([0, 2]), np.array([0, 4]),
+                                    np.zeros((2, 2), np.int32), np.zeros((2, 40), np.int32))
+    assert pbm.tolist() == [[0, 0], [2, 2]]  # 33 -> word 1 bit 1; 1 -> word 0 bit 1
+    assert obc[1, :6].tolist() == [0, 1, 0, 0, 0, 1] and obc[0].sum() == 0
+    # bit 31 sets the sign bit; tokens past the mask or the vocabulary are skipped
+    pbm, obc = oracle.vllm_bincount(np.array([0]), np.array([[31, 64, 40, 7]]), np.array([2]), np.array([4]),
+                                    np.zeros((1, 2), np.int32), np.zeros((1, 16), np.int32))
+    assert pbm.tolist() == [[-(2 ** 31), 0]]
+    assert obc[0].tolist() == [0] * 7 + [1] + [0] * 8

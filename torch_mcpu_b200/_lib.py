@@ -90,6 +90,11 @@ SIGNATURES = {
     "mcpu_vllm_topk_log_softmax": (c_int, [c_void_p, c_void_p, c_int, c_int64, c_int64, c_void_p, c_int64, c_int64,
                                            c_int64, c_void_p]),
     "mcpu_vllm_ranks": (c_int, [c_void_p, c_void_p, c_int, c_int64, c_int64, c_void_p, c_int64, c_void_p]),
+    "mcpu_vllm_penalties": (c_int, [c_void_p, c_int, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p,
+                                    c_void_p, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_int64,
+                                    c_int64, c_void_p]),
+    "mcpu_vllm_bincount": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64,
+                                   c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_void_p]),
     "mcpu_device_error": (c_int, [ctypes.POINTER(c_int), c_int]),
     "mcpu_mem_get_info": (c_int, [c_int, ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(ctypes.c_size_t)]),
     "mcpu_mem_pool_reserved": (c_int, [c_int, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64)]),

@@ -7,7 +7,12 @@
 //                                 (logprob.cpp:15-69)
 //   vllm_ranks_kernel             number of logits >= the sampled token's
 //                                 (logprob.cpp:123-149)
-// Each row is split over a cluster of 8 CTAs (256 threads each): every CTA
+//   vllm_penalties_kernel         repetition / frequency / presence penalties
+//                                 in place (penalties.cpp:14-84)
+//   vllm_bincount_kernel          prompt bit mask and output token counts
+//                                 (penalties.cpp:187-246)
+// In the first three, each row is split over a cluster of 8 CTAs (256
+// threads each): every CTA
 // streams its eighth of the row (16-byte loads, four in flight per thread,
 // where the row start allows), the CTAs combine their partial maxima, sums
 // or counts through distributed shared memory in rank order, and each then
@@ -230,6 +235,125 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kThreads)
   if (part == 0 && threadIdx.x == 0) out[r] = c;
 }
 
+template <typename T>
+__device__ __forceinline__ T from_f(float v);
+template <>
+__device__ __forceinline__ float from_f<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __half from_f<__half>(float v) { return __float2half_rn(v); }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+
+// Repetition / frequency / presence penalties in place
+// (csrc/aten/vllm_kernels/penalties.cpp:14-84).  One CTA per (row, 2048
+// logits); every thread holds 8 logits and their output counts, adds the
+// row's draft tokens (token_ids[tok - pos + 1 .. tok], staged in shared
+// memory 256 at a time) to the counts, and writes each logit back once.  The
+// arithmetic is the reference's, one rounding per operation (no contraction):
+// l / rep or l * rep where the token is in the prompt or the output, then
+// l - freq * count, then l - pres * [count > 0].
+constexpr int kPenElems = 8;
+constexpr int kPenChunk = kThreads * kPenElems;
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads)
+    penalties_kernel(T* logits, long long stride, long long vocab, const int32_t* idx, const int32_t* tids,
+                     const int32_t* lpos, const float* rep, const float* freq, const float* pres,
+                     long long num_reqs, const int32_t* pbm, long long pbm_stride, const int32_t* obc,
+                     long long obc_stride, long long max_spec_len) {
+  __shared__ int32_t drafts[kThreads];
+  const long long tok = blockIdx.x;
+  const int32_t req = idx[tok];
+  if (req < 0 || req >= num_reqs) {  // the same for every CTA of the row
+    if (blockIdx.y == 0 && threadIdx.x == 0) atomicOr(&g_sampler_error, 1);
+    return;
+  }
+  const float rp = rep[req], fp = freq[req], pp = pres[req];
+  if (rp == 1.0f && fp == 0.0f && pp == 0.0f) return;
+  const int32_t pos = lpos[tok];
+  const bool use_drafts = pos > 0 && max_spec_len > 0;
+  const long long d0 = tok - pos + 1;  // first draft; the last is token tok
+  if (use_drafts && d0 < 0) {
+    if (blockIdx.y == 0 && threadIdx.x == 0) atomicOr(&g_sampler_error, 1);
+    return;
+  }
+  T* row = logits + tok * stride;
+  const int32_t* orow = obc + req * obc_stride;
+  const int32_t* prow = pbm + req * pbm_stride;
+  const long long v0 = static_cast<long long>(blockIdx.y) * kPenChunk + threadIdx.x;
+  int cnt[kPenElems];
+  float x[kPenElems];
+#pragma unroll
+  for (int j = 0; j < kPenElems; ++j) {
+    const long long v = v0 + j * kThreads;
+    cnt[j] = v < vocab ? orow[v] : 0;
+    x[j] = v < vocab ? to_f(row[v]) : 0.0f;
+  }
+  if (use_drafts) {
+    for (int base = 0; base < pos; base += kThreads) {
+      const int nd = min(kThreads, pos - base);
+      __syncthreads();
+      if (static_cast<int>(threadIdx.x) < nd) drafts[threadIdx.x] = tids[d0 + base + threadIdx.x];
+      __syncthreads();
+      for (int d = 0; d < nd; ++d) {
+        const long long t = drafts[d];
+#pragma unroll
+        for (int j = 0; j < kPenElems; ++j) cnt[j] += t == v0 + j * kThreads ? 1 : 0;
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < kPenElems; ++j) {
+    const long long v = v0 + j * kThreads;
+    if (v >= vocab) continue;
+    float l = x[j];
+    const bool in_out = cnt[j] > 0;
+    if (rp != 1.0f) {
+      const bool in_prompt = (static_cast<uint32_t>(prow[v >> 5]) >> (v & 31)) & 1u;
+      if (in_prompt || in_out) l = l > 0.0f ? __fdiv_rn(l, rp) : __fmul_rn(l, rp);
+    }
+    l = __fsub_rn(l, __fmul_rn(fp, __int2float_rn(cnt[j])));
+    l = __fsub_rn(l, __fmul_rn(pp, in_out ? 1.0f : 0.0f));
+    row[v] = from_f<T>(l);
+  }
+}
+
+// Prompt bit mask and output counts of each listed request
+// (penalties.cpp:187-246): one CTA per entry of expanded_idx_mapping; the
+// prompt tokens set bits with atomicOr, the tokens generated since prefill
+// (positions prompt_len .. prefill_len) add to the counts with atomicAdd,
+// so the integer results do not depend on the order.  Tokens outside the
+// vocabulary are skipped, as in the reference; a request index or length
+// outside its tensor sets the error flag.
+__global__ void __launch_bounds__(kThreads)
+    bincount_kernel(const int32_t* idx, const int32_t* tids, long long tids_stride, long long max_seq,
+                    const int32_t* plen, const int32_t* flen, long long num_reqs, int32_t* pbm,
+                    long long packed_cols, long long pbm_stride, int32_t* obc, long long vocab,
+                    long long obc_stride) {
+  const int32_t req = idx[blockIdx.x];
+  if (req < 0 || req >= num_reqs) {
+    if (threadIdx.x == 0) atomicOr(&g_sampler_error, 1);
+    return;
+  }
+  long long p = plen[req], f = flen[req];
+  if (p < 0 || f > max_seq) {
+    if (threadIdx.x == 0) atomicOr(&g_sampler_error, 1);
+    p = max(p, 0LL);
+    f = min(f, max_seq);
+  }
+  const int32_t* trow = tids + req * tids_stride;
+  int32_t* prow = pbm + req * pbm_stride;
+  int32_t* orow = obc + req * obc_stride;
+  for (long long i = threadIdx.x; i < min(p, max_seq); i += kThreads) {
+    const int32_t t = trow[i];
+    if (t >= 0 && t / 32 < packed_cols) atomicOr(&prow[t / 32], static_cast<int32_t>(1u << (t % 32)));
+  }
+  for (long long i = p + threadIdx.x; i < f; i += kThreads) {
+    const int32_t t = trow[i];
+    if (t >= 0 && t < vocab) atomicAdd(&orow[t], 1);
+  }
+}
+
 orError_t check_float(int dtype, const char* op) {
   MCPU_ARG_CHECK(dtype == MCPU_FLOAT32 || dtype == MCPU_FLOAT16 || dtype == MCPU_BFLOAT16,
                  "%s: logits must be float32, float16 or bfloat16 (dtype code %d)", op, dtype);
@@ -329,4 +453,62 @@ extern "C" orError_t mcpu_vllm_ranks(int64_t* output, const void* logits, int dt
     sampler::ranks_kernel<__nv_bfloat16><<<grid, sampler::kThreads, 0, st>>>(
         output, static_cast<const __nv_bfloat16*>(logits), logits_stride, token_ids, vocab_size);
   return from_cuda(cudaGetLastError(), "vllm_ranks_kernel launch");
+}
+
+extern "C" orError_t mcpu_vllm_penalties(void* logits, int dtype, int64_t num_tokens, int64_t logits_stride,
+                                         const int32_t* expanded_idx_mapping, const int32_t* token_ids,
+                                         const int32_t* expanded_local_pos, const float* repetition_penalty,
+                                         const float* frequency_penalty, const float* presence_penalty,
+                                         int64_t max_num_reqs, const int32_t* prompt_bin_mask, int64_t pbm_stride,
+                                         const int32_t* output_bin_counts, int64_t obc_stride, int64_t vocab_size,
+                                         int64_t max_spec_len, orStream_t stream) {
+  orError_t e = sampler::check_float(dtype, "vllm_penalties_kernel");
+  if (e != orSuccess) return e;
+  MCPU_ARG_CHECK(num_tokens >= 0 && num_tokens < (1LL << 31), "vllm_penalties_kernel: bad num_tokens");
+  MCPU_ARG_CHECK(vocab_size > 0 && vocab_size <= logits_stride && vocab_size <= obc_stride &&
+                     vocab_size <= pbm_stride * 32 && vocab_size < (1LL << 31),
+                 "vllm_penalties_kernel: vocab_size %lld out of range", static_cast<long long>(vocab_size));
+  MCPU_ARG_CHECK(max_num_reqs > 0, "vllm_penalties_kernel: no requests");
+  if (num_tokens == 0) return orSuccess;
+  MCPU_ARG_CHECK(logits && expanded_idx_mapping && token_ids && expanded_local_pos && repetition_penalty &&
+                     frequency_penalty && presence_penalty && prompt_bin_mask && output_bin_counts,
+                 "vllm_penalties_kernel: NULL pointer");
+  const int64_t chunks = (vocab_size + sampler::kPenChunk - 1) / sampler::kPenChunk;
+  MCPU_ARG_CHECK(chunks <= 65535, "vllm_penalties_kernel: vocab_size too large");
+  const dim3 grid(static_cast<unsigned>(num_tokens), static_cast<unsigned>(chunks));
+  cudaStream_t st = as_cuda(stream);
+#define MCPU_PENALTIES(T)                                                                                      \
+  sampler::penalties_kernel<T><<<grid, sampler::kThreads, 0, st>>>(                                            \
+      static_cast<T*>(logits), logits_stride, vocab_size, expanded_idx_mapping, token_ids, expanded_local_pos, \
+      repetition_penalty, frequency_penalty, presence_penalty, max_num_reqs, prompt_bin_mask, pbm_stride,      \
+      output_bin_counts, obc_stride, max_spec_len)
+  if (dtype == MCPU_FLOAT32)
+    MCPU_PENALTIES(float);
+  else if (dtype == MCPU_FLOAT16)
+    MCPU_PENALTIES(__half);
+  else
+    MCPU_PENALTIES(__nv_bfloat16);
+#undef MCPU_PENALTIES
+  return from_cuda(cudaGetLastError(), "vllm_penalties_kernel launch");
+}
+
+extern "C" orError_t mcpu_vllm_bincount(const int32_t* expanded_idx_mapping, int64_t num_reqs,
+                                        const int32_t* all_token_ids, int64_t tids_stride, int64_t max_seq_len,
+                                        const int32_t* prompt_len, const int32_t* prefill_len, int64_t max_num_reqs,
+                                        int32_t* prompt_bin_mask, int64_t packed_cols, int64_t pbm_stride,
+                                        int32_t* output_bin_counts, int64_t vocab_size, int64_t obc_stride,
+                                        orStream_t stream) {
+  MCPU_ARG_CHECK(num_reqs >= 0 && num_reqs < (1LL << 31), "vllm_bincount_kernel: bad num_reqs");
+  MCPU_ARG_CHECK(max_seq_len >= 0 && max_seq_len <= tids_stride && packed_cols >= 0 && packed_cols <= pbm_stride &&
+                     vocab_size >= 0 && vocab_size <= obc_stride,
+                 "vllm_bincount_kernel: sizes exceed their strides");
+  if (num_reqs == 0) return orSuccess;
+  MCPU_ARG_CHECK(max_num_reqs > 0, "vllm_bincount_kernel: no requests");
+  MCPU_ARG_CHECK(expanded_idx_mapping && all_token_ids && prompt_len && prefill_len && prompt_bin_mask &&
+                     output_bin_counts,
+                 "vllm_bincount_kernel: NULL pointer");
+  sampler::bincount_kernel<<<static_cast<unsigned>(num_reqs), sampler::kThreads, 0, as_cuda(stream)>>>(
+      expanded_idx_mapping, all_token_ids, tids_stride, max_seq_len, prompt_len, prefill_len, max_num_reqs,
+      prompt_bin_mask, packed_cols, pbm_stride, output_bin_counts, vocab_size, obc_stride);
+  return from_cuda(cudaGetLastError(), "vllm_bincount_kernel launch");
 }

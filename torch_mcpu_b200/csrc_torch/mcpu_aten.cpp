@@ -18,6 +18,7 @@
 #include <c10/core/ScalarType.h>
 #include <torch/library.h>
 
+#include <algorithm>
 #include <cstring>
 #include <vector>
 
@@ -697,6 +698,78 @@ void vllm_ranks_kernel(at::Tensor& output, const at::Tensor& logits, const at::T
           "vllm_ranks_kernel");
 }
 
+// csrc/aten/vllm_kernels/penalties.cpp:87-118 (checks) and 248-272 (schemas)
+void vllm_penalties_kernel(at::Tensor& logits, const at::Tensor& expanded_idx_mapping,
+                           const at::Tensor& token_ids, const at::Tensor& expanded_local_pos,
+                           const at::Tensor& repetition_penalty, const at::Tensor& frequency_penalty,
+                           const at::Tensor& presence_penalty, const at::Tensor& prompt_bin_mask,
+                           const at::Tensor& output_bin_counts, int64_t vocab_size, int64_t max_spec_len) {
+  TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "logits must be 2-D with unit column stride");
+  const int dt = sampler_dtype(logits, "logits");
+  auto int1d = [](const at::Tensor& t, const char* name) {
+    TORCH_CHECK(t.dim() == 1 && t.scalar_type() == at::kInt, name, " must be 1-D int32");
+    return t.contiguous();
+  };
+  auto float1d = [](const at::Tensor& t, const char* name) {
+    TORCH_CHECK(t.dim() == 1 && t.scalar_type() == at::kFloat, name, " must be 1-D float32");
+    return t.contiguous();
+  };
+  const at::Tensor idx = int1d(expanded_idx_mapping, "expanded_idx_mapping");
+  const at::Tensor tids = int1d(token_ids, "token_ids");
+  const at::Tensor lpos = int1d(expanded_local_pos, "expanded_local_pos");
+  const at::Tensor rep = float1d(repetition_penalty, "repetition_penalty");
+  const at::Tensor freq = float1d(frequency_penalty, "frequency_penalty");
+  const at::Tensor pres = float1d(presence_penalty, "presence_penalty");
+  TORCH_CHECK(prompt_bin_mask.dim() == 2 && prompt_bin_mask.scalar_type() == at::kInt &&
+                  prompt_bin_mask.stride(1) == 1,
+              "prompt_bin_mask must be 2-D int32 with unit column stride");
+  TORCH_CHECK(output_bin_counts.dim() == 2 && output_bin_counts.scalar_type() == at::kInt &&
+                  output_bin_counts.stride(1) == 1,
+              "output_bin_counts must be 2-D int32 with unit column stride");
+  TORCH_CHECK(vocab_size > 0 && vocab_size <= logits.size(1) && vocab_size <= output_bin_counts.size(1) &&
+                  (vocab_size + 31) / 32 <= prompt_bin_mask.size(1),
+              "vllm_penalties_kernel: vocab_size ", vocab_size, " out of range");
+  const int64_t n = logits.size(0);
+  TORCH_CHECK(idx.numel() >= n && tids.numel() >= n && lpos.numel() >= n,
+              "vllm_penalties_kernel: per-token tensors shorter than the logits rows");
+  const int64_t reqs = std::min({rep.numel(), freq.numel(), pres.numel(), prompt_bin_mask.size(0),
+                                 output_bin_counts.size(0)});
+  MCPU_OK(mcpu_vllm_penalties(logits.data_ptr(), dt, n, logits.stride(0), idx.const_data_ptr<int32_t>(),
+                              tids.const_data_ptr<int32_t>(), lpos.const_data_ptr<int32_t>(),
+                              rep.const_data_ptr<float>(), freq.const_data_ptr<float>(),
+                              pres.const_data_ptr<float>(), reqs, prompt_bin_mask.const_data_ptr<int32_t>(),
+                              prompt_bin_mask.stride(0), output_bin_counts.const_data_ptr<int32_t>(),
+                              output_bin_counts.stride(0), vocab_size, max_spec_len, stream_of(logits)),
+          "vllm_penalties_kernel");
+}
+
+void vllm_bincount_kernel(const at::Tensor& expanded_idx_mapping, const at::Tensor& all_token_ids,
+                          const at::Tensor& prompt_len, const at::Tensor& prefill_len, at::Tensor& prompt_bin_mask,
+                          at::Tensor& output_bin_counts) {
+  auto int1d = [](const at::Tensor& t, const char* name) {
+    TORCH_CHECK(t.dim() == 1 && t.scalar_type() == at::kInt, name, " must be 1-D int32");
+    return t.contiguous();
+  };
+  auto int2d = [](const at::Tensor& t, const char* name) {
+    TORCH_CHECK(t.dim() == 2 && t.scalar_type() == at::kInt && t.stride(1) == 1, name,
+                " must be 2-D int32 with unit column stride");
+  };
+  const at::Tensor idx = int1d(expanded_idx_mapping, "expanded_idx_mapping");
+  const at::Tensor plen = int1d(prompt_len, "prompt_len");
+  const at::Tensor flen = int1d(prefill_len, "prefill_len");
+  int2d(all_token_ids, "all_token_ids");
+  int2d(prompt_bin_mask, "prompt_bin_mask");
+  int2d(output_bin_counts, "output_bin_counts");
+  const int64_t reqs = std::min({plen.numel(), flen.numel(), all_token_ids.size(0), prompt_bin_mask.size(0),
+                                 output_bin_counts.size(0)});
+  MCPU_OK(mcpu_vllm_bincount(idx.const_data_ptr<int32_t>(), idx.numel(), all_token_ids.const_data_ptr<int32_t>(),
+                             all_token_ids.stride(0), all_token_ids.size(1), plen.const_data_ptr<int32_t>(),
+                             flen.const_data_ptr<int32_t>(), reqs, prompt_bin_mask.data_ptr<int32_t>(),
+                             prompt_bin_mask.size(1), prompt_bin_mask.stride(0), output_bin_counts.data_ptr<int32_t>(),
+                             output_bin_counts.size(1), output_bin_counts.stride(0), stream_of(all_token_ids)),
+          "vllm_bincount_kernel");
+}
+
 // Row-parallel down projection + SUM all-reduce of the partials in one kernel
 // (mm, csrc/aten/ops/mm.cpp:13-51, then McpuBackend::allreduce,
 // torch_mcpu/csrc/Distributed.cpp:403-413).  `window` is the address of the
@@ -800,6 +873,12 @@ TORCH_LIBRARY_FRAGMENT(mcpu, m) {
   m.def("vllm_topk_log_softmax_kernel(Tensor(a!) output, Tensor logits, Tensor topk_ids, int topk, "
         "int vocab_size) -> ()");
   m.def("vllm_ranks_kernel(Tensor(a!) output, Tensor logits, Tensor token_ids, int vocab_size) -> ()");
+  m.def("vllm_penalties_kernel(Tensor(a!) logits, Tensor expanded_idx_mapping, Tensor token_ids, "
+        "Tensor expanded_local_pos, Tensor repetition_penalty, Tensor frequency_penalty, "
+        "Tensor presence_penalty, Tensor prompt_bin_mask, Tensor output_bin_counts, int vocab_size, "
+        "int max_spec_len) -> ()");
+  m.def("vllm_bincount_kernel(Tensor expanded_idx_mapping, Tensor all_token_ids, Tensor prompt_len, "
+        "Tensor prefill_len, Tensor(a!) prompt_bin_mask, Tensor(b!) output_bin_counts) -> ()");
   m.def("moe_align_block_size(Tensor topk_ids, int num_experts, int block_size, Tensor(a!) sorted_token_ids, "
         "Tensor(b!) experts_ids, Tensor(c!) num_tokens_post_pad) -> ()");
 }
@@ -815,5 +894,7 @@ TORCH_LIBRARY_IMPL(mcpu, PrivateUse1, m) {
   m.impl("vllm_min_p_kernel", vllm_min_p_kernel);
   m.impl("vllm_topk_log_softmax_kernel", vllm_topk_log_softmax_kernel);
   m.impl("vllm_ranks_kernel", vllm_ranks_kernel);
+  m.impl("vllm_penalties_kernel", vllm_penalties_kernel);
+  m.impl("vllm_bincount_kernel", vllm_bincount_kernel);
   m.impl("moe_align_block_size", moe_align_block_size);
 }
