@@ -333,3 +333,35 @@ def vllm_bincount(idx: np.ndarray, all_token_ids: np.ndarray, prompt_len: np.nda
         ot = np.asarray(all_token_ids[q, p:f], dtype=np.int64)
         np.add.at(obc[q], ot[(ot >= 0) & (ot < vocab)], 1)
     return pbm, obc
+
+
+def vllm_bias(logits: np.ndarray, vocab: int, idx: np.ndarray, num_allowed: np.ndarray, allowed: np.ndarray,
+              num_bias: np.ndarray, bias_ids: np.ndarray, bias: np.ndarray, pos: np.ndarray,
+              min_lens: np.ndarray, num_stop: np.ndarray, stop_ids: np.ndarray,
+              rnd=lambda v: np.float32(v)) -> np.ndarray:
+    """logit_bias.cpp:8-86, per token row in order: (1) with allowed tokens,
+    keep the values of the first min(n, 512) allowed ids (clamped into the
+    vocabulary) and set the rest of the row to -inf; (2) add each bias to its
+    id in list order, rounding to the logits dtype after each add (`rnd`);
+    (3) while pos < min_len, set the stop ids to -inf.  Values are fp32
+    copies of the logits dtype; returns new logits."""
+    lg = np.array(logits, dtype=np.float32, copy=True)
+    for t in range(lg.shape[0]):
+        q = int(idx[t])
+        row = lg[t]
+        na = int(num_allowed[q])
+        if na > 0:
+            ids = np.clip(np.asarray(allowed[q, :min(na, 512)], dtype=np.int64), 0, vocab - 1)
+            keep = row[ids].copy()
+            row[:vocab] = -np.inf
+            row[ids] = keep
+        for k in range(int(num_bias[q])):
+            i = int(bias_ids[q, k])
+            if 0 <= i < vocab:
+                row[i] = rnd(np.float32(row[i]) + np.float32(bias[q, k]))
+        if int(num_stop[q]) > 0 and int(pos[t]) < int(min_lens[q]):
+            for k in range(int(num_stop[q])):
+                i = int(stop_ids[q, k])
+                if 0 <= i < vocab:
+                    row[i] = -np.inf
+    return lg

@@ -11,6 +11,8 @@
 //                                 in place (penalties.cpp:14-84)
 //   vllm_bincount_kernel          prompt bit mask and output token counts
 //                                 (penalties.cpp:187-246)
+//   vllm_bias_kernel              allowed-token mask, logit bias, min-length
+//                                 stop tokens (logit_bias.cpp:8-86)
 // In the first three, each row is split over a cluster of 8 CTAs (256
 // threads each): every CTA
 // streams its eighth of the row (16-byte loads, four in flight per thread,
@@ -354,6 +356,77 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
+// Allowed-token masks, logit bias and min-length stop tokens
+// (logit_bias.cpp:8-86), one CTA per token row, in the reference's order
+// with a block barrier between the steps: (1) the first min(n, 512) allowed
+// ids (clamped into the vocabulary) keep their values, staged in shared
+// memory, and the rest of the row becomes -inf; (2) one thread adds the
+// biases in list order, rounding to the logits dtype after each add, so
+// repeated ids give the reference's sums; (3) while pos < min_len the stop
+// ids become -inf.  A count above its list's width is clamped and sets the
+// error flag (the reference reads past the row).
+constexpr int kMaxAllowed = 512;
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads)
+    bias_kernel(T* logits, long long stride, long long vocab, const int32_t* idx, long long num_reqs,
+                const int32_t* n_allowed, const int32_t* allowed, long long allowed_stride, long long allowed_cols,
+                const int32_t* n_bias, const int32_t* bias_ids, long long bias_ids_stride, const float* bias,
+                long long bias_stride, long long bias_cols, const int64_t* pos, const int32_t* min_lens,
+                const int32_t* n_stop, const int32_t* stop, long long stop_stride, long long stop_cols) {
+  __shared__ __align__(4) unsigned char saved_raw[kMaxAllowed * sizeof(T)];  // the values, bit for bit
+  __shared__ int32_t saved_ids[kMaxAllowed];
+  T* saved = reinterpret_cast<T*>(saved_raw);
+  const long long tok = blockIdx.x;
+  const int32_t req = idx[tok];
+  if (req < 0 || req >= num_reqs) {
+    if (threadIdx.x == 0) atomicOr(&g_sampler_error, 1);
+    return;
+  }
+  T* row = logits + tok * stride;
+  const int32_t na = n_allowed[req];
+  if (na > 0) {
+    if (na > allowed_cols && threadIdx.x == 0) atomicOr(&g_sampler_error, 1);
+    const int ns = static_cast<int>(min(min(static_cast<long long>(na), static_cast<long long>(kMaxAllowed)),
+                                        allowed_cols));
+    const int32_t* arow = allowed + req * allowed_stride;
+    for (int k = threadIdx.x; k < ns; k += kThreads) {
+      const int32_t id = min(max(arow[k], 0), static_cast<int32_t>(vocab - 1));
+      saved_ids[k] = id;
+      saved[k] = row[id];
+    }
+    __syncthreads();
+    for (long long i = threadIdx.x; i < vocab; i += kThreads) row[i] = neg_inf<T>();
+    __syncthreads();
+    // repeated ids saved the same value, so the order of these stores does not matter
+    for (int k = threadIdx.x; k < ns; k += kThreads) row[saved_ids[k]] = saved[k];
+  }
+  __syncthreads();
+  const int32_t nb = n_bias[req];
+  if (nb > 0 && threadIdx.x == 0) {
+    if (nb > bias_cols) atomicOr(&g_sampler_error, 1);
+    const long long n = min(static_cast<long long>(nb), bias_cols);
+    const int32_t* brow = bias_ids + req * bias_ids_stride;
+    const float* vrow = bias + req * bias_stride;
+    for (long long k = 0; k < n; ++k) {
+      const int32_t id = brow[k];
+      if (id < 0 || id >= vocab) continue;
+      row[id] = from_f<T>(__fadd_rn(to_f(row[id]), vrow[k]));
+    }
+  }
+  __syncthreads();
+  const int32_t nst = n_stop[req];
+  if (nst > 0 && pos[tok] < min_lens[req]) {
+    if (nst > stop_cols && threadIdx.x == 0) atomicOr(&g_sampler_error, 1);
+    const long long n = min(static_cast<long long>(nst), stop_cols);
+    const int32_t* srow = stop + req * stop_stride;
+    for (long long k = threadIdx.x; k < n; k += kThreads) {
+      const int32_t id = srow[k];
+      if (id >= 0 && id < vocab) row[id] = neg_inf<T>();
+    }
+  }
+}
+
 orError_t check_float(int dtype, const char* op) {
   MCPU_ARG_CHECK(dtype == MCPU_FLOAT32 || dtype == MCPU_FLOAT16 || dtype == MCPU_BFLOAT16,
                  "%s: logits must be float32, float16 or bfloat16 (dtype code %d)", op, dtype);
@@ -511,4 +584,43 @@ extern "C" orError_t mcpu_vllm_bincount(const int32_t* expanded_idx_mapping, int
       expanded_idx_mapping, all_token_ids, tids_stride, max_seq_len, prompt_len, prefill_len, max_num_reqs,
       prompt_bin_mask, packed_cols, pbm_stride, output_bin_counts, vocab_size, obc_stride);
   return from_cuda(cudaGetLastError(), "vllm_bincount_kernel launch");
+}
+
+extern "C" orError_t mcpu_vllm_bias(void* logits, int dtype, int64_t num_tokens, int64_t logits_stride,
+                                    int64_t vocab_size, const int32_t* expanded_idx_mapping, int64_t max_num_reqs,
+                                    const int32_t* num_allowed, const int32_t* allowed, int64_t allowed_stride,
+                                    int64_t allowed_cols, const int32_t* num_bias, const int32_t* bias_ids,
+                                    int64_t bias_ids_stride, const float* bias, int64_t bias_stride,
+                                    int64_t bias_cols, const int64_t* pos, const int32_t* min_lens,
+                                    const int32_t* num_stop, const int32_t* stop_ids, int64_t stop_stride,
+                                    int64_t stop_cols, orStream_t stream) {
+  orError_t e = sampler::check_float(dtype, "vllm_bias_kernel");
+  if (e != orSuccess) return e;
+  MCPU_ARG_CHECK(num_tokens >= 0 && num_tokens < (1LL << 31), "vllm_bias_kernel: bad num_tokens");
+  MCPU_ARG_CHECK(vocab_size > 0 && vocab_size <= logits_stride && vocab_size < (1LL << 31),
+                 "vllm_bias_kernel: vocab_size %lld out of range", static_cast<long long>(vocab_size));
+  MCPU_ARG_CHECK(allowed_cols >= 0 && allowed_cols <= allowed_stride && bias_cols >= 0 &&
+                     bias_cols <= bias_ids_stride && bias_cols <= bias_stride && stop_cols >= 0 &&
+                     stop_cols <= stop_stride,
+                 "vllm_bias_kernel: list widths exceed their strides");
+  if (num_tokens == 0) return orSuccess;
+  MCPU_ARG_CHECK(max_num_reqs > 0, "vllm_bias_kernel: no requests");
+  MCPU_ARG_CHECK(logits && expanded_idx_mapping && num_allowed && allowed && num_bias && bias_ids && bias && pos &&
+                     min_lens && num_stop && stop_ids,
+                 "vllm_bias_kernel: NULL pointer");
+  const dim3 grid(static_cast<unsigned>(num_tokens));
+  cudaStream_t st = as_cuda(stream);
+#define MCPU_BIAS(T)                                                                                               \
+  sampler::bias_kernel<T><<<grid, sampler::kThreads, 0, st>>>(                                                     \
+      static_cast<T*>(logits), logits_stride, vocab_size, expanded_idx_mapping, max_num_reqs, num_allowed, allowed, \
+      allowed_stride, allowed_cols, num_bias, bias_ids, bias_ids_stride, bias, bias_stride, bias_cols, pos,         \
+      min_lens, num_stop, stop_ids, stop_stride, stop_cols)
+  if (dtype == MCPU_FLOAT32)
+    MCPU_BIAS(float);
+  else if (dtype == MCPU_FLOAT16)
+    MCPU_BIAS(__half);
+  else
+    MCPU_BIAS(__nv_bfloat16);
+#undef MCPU_BIAS
+  return from_cuda(cudaGetLastError(), "vllm_bias_kernel launch");
 }
