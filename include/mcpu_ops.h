@@ -325,6 +325,27 @@ OPENREG_EXPORT orError_t mcpu_vllm_bincount(const int32_t* expanded_idx_mapping,
                                             int32_t* output_bin_counts, int64_t vocab_size, int64_t obc_stride,
                                             orStream_t stream);
 
+/*
+ * Logit bias (logit_bias.cpp:15-96, mcpu::vllm_bias_kernel), per token row t
+ *   with request q = expanded_idx_mapping[t], in this order: (1) when
+ *   num_allowed[q] = n > 0, the first min(n, 512) ids of allowed row q
+ *   (clamped into [0, vocab)) keep their values and every other entry of the
+ *   row becomes -inf; (2) bias[q, k] is added to logit bias_ids[q, k] for
+ *   k < num_bias[q] in list order, rounded to the logits dtype after each
+ *   add, ids outside the vocab skipped; (3) when pos[t] (int64) <
+ *   min_lens[q], the first num_stop[q] stop ids become -inf.  A request index
+ *   out of range leaves the row, and a count above its list's width is
+ *   clamped; both set mcpu_device_error.
+ */
+OPENREG_EXPORT orError_t mcpu_vllm_bias(void* logits, int dtype, int64_t num_tokens, int64_t logits_stride,
+                                        int64_t vocab_size, const int32_t* expanded_idx_mapping,
+                                        int64_t max_num_reqs, const int32_t* num_allowed, const int32_t* allowed,
+                                        int64_t allowed_stride, int64_t allowed_cols, const int32_t* num_bias,
+                                        const int32_t* bias_ids, int64_t bias_ids_stride, const float* bias,
+                                        int64_t bias_stride, int64_t bias_cols, const int64_t* pos,
+                                        const int32_t* min_lens, const int32_t* num_stop, const int32_t* stop_ids,
+                                        int64_t stop_stride, int64_t stop_cols, orStream_t stream);
+
 /* *flag = 1 if a kernel on the current device (tensor-core GEMM, TMA-fed
  * router or bulk-copy-fed rms_norm) gave up on a bounded wait, or a gather /
  * scatter met an index out of range, since the last reset; that launch left

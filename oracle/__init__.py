@@ -339,7 +339,7 @@ def vllm_bias(logits: np.ndarray, vocab: int, idx: np.ndarray, num_allowed: np.n
               num_bias: np.ndarray, bias_ids: np.ndarray, bias: np.ndarray, pos: np.ndarray,
               min_lens: np.ndarray, num_stop: np.ndarray, stop_ids: np.ndarray,
               rnd=lambda v: np.float32(v)) -> np.ndarray:
-    """logit_bias.cpp:8-86, per token row in order: (1) with allowed tokens,
+    """logit_bias.cpp:15-96, per token row in order: (1) with allowed tokens,
     keep the values of the first min(n, 512) allowed ids (clamped into the
     vocabulary) and set the rest of the row to -inf; (2) add each bias to its
     id in list order, rounding to the logits dtype after each add (`rnd`);

@@ -1,14 +1,15 @@
 """The reference's vLLM sampler ops (mcpu::vllm_min_p_kernel,
 vllm_topk_log_softmax_kernel, vllm_ranks_kernel; csrc/aten/vllm_kernels/
 min_p.cpp, logprob.cpp; vllm_penalties_kernel, vllm_bincount_kernel:
-penalties.cpp) on the B200 against the oracle, called as the
+penalties.cpp; vllm_bias_kernel: logit_bias.cpp) on the B200 against the
+oracle, called as the
 reference's users call them (torch.ops.mcpu on mcpu tensors): fp32, fp16
 and bf16 logits, vocabularies with 16-byte-aligned and unaligned rows, a
 row stride wider than the vocabulary, -inf and NaN entries, p = 0 rows and
 out-of-range ids.  ranks are exact; log-probabilities within 2e-6; min_p
 results identical except where an entry lies within one fp32 ulp of the
 threshold (the threshold's logarithm is rounded once from fp64); penalties
-and bincount bit-exact."""
+, bincount and bias bit-exact."""
 
 import numpy as np
 import pytest
@@ -159,3 +160,49 @@ def test_penalties_bad_request_index(mcpu):
     assert torch.equal(got[1], torch.ones(64))  # request 7 of 1: the row is left, the flag set
     assert torch.equal(got[0], torch.full((64,), 0.5))  # all in the prompt: 1 / 2
     assert device_error(reset=True) == 1
+
+
+def _rounder(dtype):
+    if dtype == torch.float32:
+        return lambda v: np.float32(v)
+    if dtype == torch.float16:
+        return lambda v: np.float32(np.float16(np.float32(v)))
+    return lambda v: oracle.bf16_bits_to_f32(oracle.f32_to_bf16_bits(np.array([v], dtype=np.float32)))[0]
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("width,vocab", [(32000, 32000), (151937, 151937), (50016, 50000)])
+def test_bias(mcpu, dtype, width, vocab):
+    """Allowed lists (empty, clamped ids, longer than the 512 kept), repeated
+    bias ids (summed in list order with a rounding per add), biases on masked
+    and out-of-vocabulary ids, stop ids before and after min_len."""
+    g = torch.Generator().manual_seed(6)
+    reqs = 5
+    na = torch.tensor([0, 3, 600, 0, 1], dtype=torch.int32)
+    allowed = torch.randint(0, vocab, (reqs, 640), generator=g, dtype=torch.int32)
+    allowed[1, :3] = torch.tensor([5, -4, vocab + 3], dtype=torch.int32)
+    nb = torch.tensor([4, 2, 0, 16, 3], dtype=torch.int32)
+    bias_ids = torch.randint(0, vocab, (reqs, 16), generator=g, dtype=torch.int32)
+    bias_ids[0, :4] = torch.tensor([10, 10, vocab + 1, 11], dtype=torch.int32)
+    bias_ids[1, :2] = torch.tensor([5, 6], dtype=torch.int32)
+    bias = (0.3 * torch.randn(reqs, 16, generator=g)).float()
+    bias[0, :2] = torch.tensor([1e-3, 3.0e-3])
+    ml = torch.tensor([4, 0, 10, 3, 2], dtype=torch.int32)
+    ns = torch.tensor([2, 4, 1, 0, 3], dtype=torch.int32)
+    stop = torch.randint(-1, vocab + 1, (reqs, 4), generator=g, dtype=torch.int32)
+    idx = torch.tensor([0, 1, 2, 3, 4, 0, 2, 4], dtype=torch.int32)
+    pos = torch.tensor([1, 0, 9, 5, 1, 7, 12, 2], dtype=torch.int64)
+    x = _logits(idx.numel(), width, dtype, 7)
+    x[1, 7] = 1.0  # no NaN: the reference's NaN conversion to 16-bit types is not CUDA's
+    xm = x.to("mcpu")
+    m = lambda t: t.to("mcpu")  # noqa: E731
+    torch.ops.mcpu.vllm_bias_kernel(xm, vocab, m(idx), m(na), m(allowed), m(nb), m(bias_ids), m(bias), m(pos),
+                                    m(ml), m(ns), m(stop))
+    want = oracle.vllm_bias(x.float().numpy(), vocab, idx.numpy(), na.numpy(), allowed.numpy(), nb.numpy(),
+                            bias_ids.numpy(), bias.numpy(), pos.numpy(), ml.numpy(), ns.numpy(), stop.numpy(),
+                            rnd=_rounder(dtype))
+    got = xm.cpu()
+    want = torch.from_numpy(want).to(dtype)
+    iv = torch.int32 if dtype == torch.float32 else torch.int16
+    assert torch.equal(got.view(iv), want.view(iv))
+    assert int(torch.isfinite(got[2, :vocab].float()).sum()) <= 512  # the allowed list keeps at most 512

@@ -69,3 +69,19 @@ def test_bincount_known_answers():
                                     np.zeros((1, 2), np.int32), np.zeros((1, 16), np.int32))
     assert pbm.tolist() == [[-(2 ** 31), 0]]
     assert obc[0].tolist() == [0] * 7 + [1] + [0] * 8
+
+
+def test_bias_known_answers():
+    """logit_bias.cpp:15-96 by hand: allowed ids [3, 9 -> clamped to 3], bias
+    +0.5 and +0.25 on id 3 (in order) and +7 on a masked id, stop id 1 while
+    pos 1 < min_len 5."""
+    lg = np.array([[1.0, 2.0, 3.0, 4.0]], dtype=np.float32)
+    args = (4, np.array([0]), np.array([2]), np.array([[3, 9]]), np.array([3]), np.array([[3, 3, 0]]),
+            np.array([[0.5, 0.25, 7.0]], dtype=np.float32))
+    out = oracle.vllm_bias(lg, *args, np.array([1]), np.array([5]), np.array([1]), np.array([[1]]))
+    assert out.tolist() == [[-np.inf, -np.inf, -np.inf, 4.75]]
+    # no allowed list, pos past min_len: only the biases
+    out = oracle.vllm_bias(lg, 4, np.array([0]), np.array([0]), np.array([[0, 0]]), np.array([2]),
+                           np.array([[2, -1, 0]]), np.array([[0.5, 9.0, 0.0]], dtype=np.float32),
+                           np.array([5]), np.array([5]), np.array([1]), np.array([[1]]))
+    assert out.tolist() == [[1.0, 2.0, 3.5, 4.0]]

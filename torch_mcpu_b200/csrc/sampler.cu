@@ -12,7 +12,7 @@
 //   vllm_bincount_kernel          prompt bit mask and output token counts
 //                                 (penalties.cpp:187-246)
 //   vllm_bias_kernel              allowed-token mask, logit bias, min-length
-//                                 stop tokens (logit_bias.cpp:8-86)
+//                                 stop tokens (logit_bias.cpp:15-96)
 // In the first three, each row is split over a cluster of 8 CTAs (256
 // threads each): every CTA
 // streams its eighth of the row (16-byte loads, four in flight per thread,
@@ -357,7 +357,7 @@ __global__ void __launch_bounds__(kThreads)
 }
 
 // Allowed-token masks, logit bias and min-length stop tokens
-// (logit_bias.cpp:8-86), one CTA per token row, in the reference's order
+// (logit_bias.cpp:15-96), one CTA per token row, in the reference's order
 // with a block barrier between the steps: (1) the first min(n, 512) allowed
 // ids (clamped into the vocabulary) keep their values, staged in shared
 // memory, and the rest of the row becomes -inf; (2) one thread adds the

@@ -770,6 +770,51 @@ void vllm_bincount_kernel(const at::Tensor& expanded_idx_mapping, const at::Tens
           "vllm_bincount_kernel");
 }
 
+// csrc/aten/vllm_kernels/logit_bias.cpp:98-191 (checks) and 195-211 (schema)
+void vllm_bias_kernel(at::Tensor& logits, int64_t vocab_size, const at::Tensor& expanded_idx_mapping,
+                      const at::Tensor& num_allowed_token_ids, const at::Tensor& allowed_token_ids,
+                      const at::Tensor& num_logit_bias, const at::Tensor& bias_token_ids, const at::Tensor& bias,
+                      const at::Tensor& pos, const at::Tensor& min_lens, const at::Tensor& num_stop_token_ids,
+                      const at::Tensor& stop_token_ids) {
+  TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "logits must be 2-D with unit column stride");
+  const int dt = sampler_dtype(logits, "logits");
+  TORCH_CHECK(vocab_size > 0 && vocab_size <= logits.size(1), "vllm_bias_kernel: vocab_size ", vocab_size,
+              " out of range");
+  auto int1d = [](const at::Tensor& t, const char* name) {
+    TORCH_CHECK(t.dim() == 1 && t.scalar_type() == at::kInt, name, " must be 1-D int32");
+    return t.contiguous();
+  };
+  auto list2d = [](const at::Tensor& t, at::ScalarType dt2, const char* name) {
+    TORCH_CHECK(t.dim() == 2 && t.scalar_type() == dt2 && t.stride(1) == 1, name,
+                " must be 2-D with unit column stride and dtype ", dt2);
+  };
+  const at::Tensor idx = int1d(expanded_idx_mapping, "expanded_idx_mapping");
+  const at::Tensor na = int1d(num_allowed_token_ids, "num_allowed_token_ids");
+  const at::Tensor nb = int1d(num_logit_bias, "num_logit_bias");
+  const at::Tensor ml = int1d(min_lens, "min_lens");
+  const at::Tensor ns = int1d(num_stop_token_ids, "num_stop_token_ids");
+  TORCH_CHECK(pos.dim() == 1 && pos.scalar_type() == at::kLong, "pos must be 1-D int64");
+  const at::Tensor ps = pos.contiguous();
+  list2d(allowed_token_ids, at::kInt, "allowed_token_ids");
+  list2d(bias_token_ids, at::kInt, "bias_token_ids");
+  list2d(bias, at::kFloat, "bias");
+  list2d(stop_token_ids, at::kInt, "stop_token_ids");
+  TORCH_CHECK(bias.size(1) == bias_token_ids.size(1), "bias and bias_token_ids differ in width");
+  const int64_t n = logits.size(0);
+  TORCH_CHECK(idx.numel() >= n && ps.numel() >= n, "vllm_bias_kernel: per-token tensors shorter than the rows");
+  const int64_t reqs = std::min({na.numel(), nb.numel(), ml.numel(), ns.numel(), allowed_token_ids.size(0),
+                                 bias_token_ids.size(0), bias.size(0), stop_token_ids.size(0)});
+  MCPU_OK(mcpu_vllm_bias(logits.data_ptr(), dt, n, logits.stride(0), vocab_size, idx.const_data_ptr<int32_t>(), reqs,
+                         na.const_data_ptr<int32_t>(), allowed_token_ids.const_data_ptr<int32_t>(),
+                         allowed_token_ids.stride(0), allowed_token_ids.size(1), nb.const_data_ptr<int32_t>(),
+                         bias_token_ids.const_data_ptr<int32_t>(), bias_token_ids.stride(0),
+                         bias.const_data_ptr<float>(), bias.stride(0), bias.size(1), ps.const_data_ptr<int64_t>(),
+                         ml.const_data_ptr<int32_t>(), ns.const_data_ptr<int32_t>(),
+                         stop_token_ids.const_data_ptr<int32_t>(), stop_token_ids.stride(0), stop_token_ids.size(1),
+                         stream_of(logits)),
+          "vllm_bias_kernel");
+}
+
 // Row-parallel down projection + SUM all-reduce of the partials in one kernel
 // (mm, csrc/aten/ops/mm.cpp:13-51, then McpuBackend::allreduce,
 // torch_mcpu/csrc/Distributed.cpp:403-413).  `window` is the address of the
@@ -877,6 +922,9 @@ TORCH_LIBRARY_FRAGMENT(mcpu, m) {
         "Tensor expanded_local_pos, Tensor repetition_penalty, Tensor frequency_penalty, "
         "Tensor presence_penalty, Tensor prompt_bin_mask, Tensor output_bin_counts, int vocab_size, "
         "int max_spec_len) -> ()");
+  m.def("vllm_bias_kernel(Tensor(a!) logits, int vocab_size, Tensor expanded_idx_mapping, "
+        "Tensor num_allowed_token_ids, Tensor allowed_token_ids, Tensor num_logit_bias, Tensor bias_token_ids, "
+        "Tensor bias, Tensor pos, Tensor min_lens, Tensor num_stop_token_ids, Tensor stop_token_ids) -> ()");
   m.def("vllm_bincount_kernel(Tensor expanded_idx_mapping, Tensor all_token_ids, Tensor prompt_len, "
         "Tensor prefill_len, Tensor(a!) prompt_bin_mask, Tensor(b!) output_bin_counts) -> ()");
   m.def("moe_align_block_size(Tensor topk_ids, int num_experts, int block_size, Tensor(a!) sorted_token_ids, "
@@ -896,5 +944,6 @@ TORCH_LIBRARY_IMPL(mcpu, PrivateUse1, m) {
   m.impl("vllm_ranks_kernel", vllm_ranks_kernel);
   m.impl("vllm_penalties_kernel", vllm_penalties_kernel);
   m.impl("vllm_bincount_kernel", vllm_bincount_kernel);
+  m.impl("vllm_bias_kernel", vllm_bias_kernel);
   m.impl("moe_align_block_size", moe_align_block_size);
 }
