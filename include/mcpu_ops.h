@@ -346,6 +346,27 @@ OPENREG_EXPORT orError_t mcpu_vllm_bias(void* logits, int dtype, int64_t num_tok
                                         const int32_t* min_lens, const int32_t* num_stop, const int32_t* stop_ids,
                                         int64_t stop_stride, int64_t stop_cols, orStream_t stream);
 
+/*
+ * Bad words (bad_words.cpp:13-82, mcpu::vllm_bad_words_kernel): for token row
+ *   t with request q and local position pos, each of the num_bad_words[q]
+ *   words w = bad_word_token_ids[q, off[w] .. off[w+1]) (off = row q of
+ *   bad_word_offsets) whose prefix (all ids but the last) equals the last
+ *   tokens of q's output all_token_ids[q, prompt_len[q] .. total_len[q])
+ *   followed by the drafts input_ids[t-pos .. t) gets its last id set to
+ *   -inf in the row.  Indexes that would leave their tensors set
+ *   mcpu_device_error and skip the word or row.
+ */
+OPENREG_EXPORT orError_t mcpu_vllm_bad_words(void* logits, int dtype, int64_t num_tokens, int64_t logits_stride,
+                                             int64_t vocab_size, const int32_t* expanded_idx_mapping,
+                                             int64_t max_num_reqs, const int32_t* bad_word_token_ids,
+                                             int64_t bw_ids_stride, int64_t bw_ids_cols,
+                                             const int32_t* bad_word_offsets, int64_t bw_off_stride,
+                                             int64_t bw_off_cols, const int32_t* num_bad_words,
+                                             const int32_t* all_token_ids, int64_t token_ids_stride,
+                                             int64_t max_seq_len, const int32_t* prompt_len,
+                                             const int32_t* total_len, const int32_t* input_ids,
+                                             const int32_t* expanded_local_pos, orStream_t stream);
+
 /* *flag = 1 if a kernel on the current device (tensor-core GEMM, TMA-fed
  * router or bulk-copy-fed rms_norm) gave up on a bounded wait, or a gather /
  * scatter met an index out of range, since the last reset; that launch left

@@ -365,3 +365,36 @@ def vllm_bias(logits: np.ndarray, vocab: int, idx: np.ndarray, num_allowed: np.n
                 if 0 <= i < vocab:
                     row[i] = -np.inf
     return lg
+
+
+def vllm_bad_words(logits: np.ndarray, idx: np.ndarray, bw_ids: np.ndarray, bw_off: np.ndarray, n_bw: np.ndarray,
+                   all_token_ids: np.ndarray, prompt_len: np.ndarray, total_len: np.ndarray,
+                   input_ids: np.ndarray, local_pos: np.ndarray) -> np.ndarray:
+    """bad_words.cpp:13-82: for token row t (request q, local position pos),
+    every bad word ids[off[w] .. off[w+1]) whose prefix equals the last
+    tokens of q's output (all_token_ids[q, prompt_len .. total_len)) followed
+    by the drafts input_ids[t-pos .. t) bans its last id (-inf).  Returns
+    new logits; the vocabulary is the row width."""
+    lg = np.array(logits, dtype=np.float32, copy=True)
+    vocab = lg.shape[1]
+    for t in range(lg.shape[0]):
+        q = int(idx[t])
+        nw = int(n_bw[q])
+        if nw == 0:
+            continue
+        pos = int(local_pos[t])
+        pl, tl = int(prompt_len[q]), int(total_len[q])
+        out_len = tl - pl
+        eff = out_len + pos
+        seq = list(all_token_ids[q, pl:tl]) + list(input_ids[t - pos:t])
+        for w in range(nw):
+            start, end = int(bw_off[q, w]), int(bw_off[q, w + 1])
+            prefix = end - start - 1
+            if prefix > eff:
+                continue
+            want = [int(v) for v in bw_ids[q, start:start + max(prefix, 0)]]
+            have = [int(v) for v in seq[eff - max(prefix, 0):eff]] if prefix > 0 else []
+            last = int(bw_ids[q, end - 1])
+            if want == have and 0 <= last < vocab:
+                lg[t, last] = -np.inf
+    return lg

@@ -1,14 +1,15 @@
 """The reference's vLLM sampler ops (mcpu::vllm_min_p_kernel,
 vllm_topk_log_softmax_kernel, vllm_ranks_kernel; csrc/aten/vllm_kernels/
 min_p.cpp, logprob.cpp; vllm_penalties_kernel, vllm_bincount_kernel:
-penalties.cpp; vllm_bias_kernel: logit_bias.cpp) on the B200 against the
+penalties.cpp; vllm_bias_kernel: logit_bias.cpp; vllm_bad_words_kernel:
+bad_words.cpp) on the B200 against the
 oracle, called as the reference's users call them (torch.ops.mcpu on mcpu tensors): fp32, fp16
 and bf16 logits, vocabularies with 16-byte-aligned and unaligned rows, a
 row stride wider than the vocabulary, -inf and NaN entries, p = 0 rows and
 out-of-range ids.  ranks are exact; log-probabilities within 2e-6; min_p
 results identical except where an entry lies within one fp32 ulp of the
 threshold (the threshold's logarithm is rounded once from fp64); penalties,
-bincount and bias bit-exact."""
+bincount, bias and bad words bit-exact."""
 
 import numpy as np
 import pytest
@@ -205,3 +206,52 @@ def test_bias(mcpu, dtype, width, vocab):
     iv = torch.int32 if dtype == torch.float32 else torch.int16
     assert torch.equal(got.view(iv), want.view(iv))
     assert int(torch.isfinite(got[2, :vocab].float()).sum()) <= 512  # the allowed list keeps at most 512
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("width,vocab", [(32000, 32000), (50016, 50000)])
+def test_bad_words(mcpu, dtype, width, vocab):
+    """Bad words built from each row's own sequence tail (output tokens, then
+    drafts), single-id words, a prefix longer than the sequence, a request
+    without bad words, ids past the vocabulary."""
+    g = torch.Generator().manual_seed(8)
+    reqs, seq = 4, 64
+    tids = torch.randint(0, 50, (reqs, seq), generator=g, dtype=torch.int32)
+    pl = torch.tensor([10, 4, 7, 20], dtype=torch.int32)
+    tl = torch.tensor([30, 9, 7, 33], dtype=torch.int32)  # request 2 has no output yet
+    idx = torch.tensor([0, 0, 0, 1, 2, 3, 3], dtype=torch.int32)
+    lpos = torch.tensor([0, 1, 2, 0, 0, 0, 1], dtype=torch.int32)
+    inp = torch.randint(0, 50, (idx.numel(),), generator=g, dtype=torch.int32)
+    out = lambda q: tids[q, int(pl[q]):int(tl[q])].tolist()  # noqa: E731
+    words = {
+        0: [[inp[0].item(), inp[1].item(), 17], [out(0)[-1], 23], [5], [1, 2, 3, 4], [vocab + 5]],
+        1: [],
+        2: [[3, 9], [11]],
+        3: [[inp[5].item(), 31], [out(3)[-2], out(3)[-1], 44], [48, 49, 0, 1]],
+    }
+    ids = torch.zeros(reqs, 16, dtype=torch.int32)
+    off = torch.zeros(reqs, 7, dtype=torch.int32)
+    nbw = torch.zeros(reqs, dtype=torch.int32)
+    for q, ws in words.items():
+        flat = [v for w in ws for v in w]
+        ids[q, :len(flat)] = torch.tensor(flat, dtype=torch.int32) if flat else ids[q, :0]
+        o = [0]
+        for w in ws:
+            o.append(o[-1] + len(w))
+        off[q, :len(o)] = torch.tensor(o, dtype=torch.int32)
+        nbw[q] = len(ws)
+    xf = _logits(idx.numel(), width, dtype, 9)
+    xf[1, 7] = 1.0
+    x = xf[:, :vocab]  # a row stride wider than the vocabulary
+    xm = xf.to("mcpu")[:, :vocab]
+    m = lambda t: t.to("mcpu")  # noqa: E731
+    torch.ops.mcpu.vllm_bad_words_kernel(xm, m(idx), m(ids), m(off), m(nbw), m(tids), m(pl), m(tl), m(inp),
+                                         m(lpos))
+    want = oracle.vllm_bad_words(x.float().numpy(), idx.numpy(), ids.numpy(), off.numpy(), nbw.numpy(),
+                                 tids.numpy(), pl.numpy(), tl.numpy(), inp.numpy(), lpos.numpy())
+    got = xm.cpu()
+    want = torch.from_numpy(want).to(dtype)
+    iv = torch.int32 if dtype == torch.float32 else torch.int16
+    assert torch.equal(got.contiguous().view(iv), want.view(iv))
+    banned = torch.isneginf(got.float()) & ~torch.isneginf(x.float())
+    assert banned[2, 17] and banned[0, 23] and banned[6, 31] and banned[5, 44] and banned[4, 11]

@@ -85,3 +85,23 @@ def test_bias_known_answers():
                            np.array([[2, -1, 0]]), np.array([[0.5, 9.0, 0.0]], dtype=np.float32),
                            np.array([5]), np.array([5]), np.array([1]), np.array([[1]]))
     assert out.tolist() == [[1.0, 2.0, 3.5, 4.0]]
+
+
+def test_bad_words_known_answers():
+    """bad_words.cpp:13-82 by hand: output so far [7, 8], bad words [8, 3]
+    (prefix 8 ends the output: bans 3), [7, 9, 4] (prefix 7 9 does not: 4
+    stays) and [5] (no prefix: always bans 5)."""
+    lg = np.zeros((1, 10), dtype=np.float32)
+    ids = np.array([[8, 3, 7, 9, 4, 5]])
+    off = np.array([[0, 2, 5, 6]])
+    tids = np.array([[1, 2, 7, 8, 0]])  # prompt [1, 2], output [7, 8]
+    out = oracle.vllm_bad_words(lg, np.array([0]), ids, off, np.array([3]), tids, np.array([2]), np.array([4]),
+                                np.array([0]), np.array([0]))
+    assert np.isneginf(out[0]).nonzero()[0].tolist() == [3, 5]
+    # two rows of one request: row 1 (pos 1) sees the output then the draft
+    # input_ids[0] = 9, so [9, 4] bans 4 there and [8, 3] bans 3 on row 0
+    out = oracle.vllm_bad_words(np.zeros((2, 10), np.float32), np.array([0, 0]), np.array([[9, 4, 8, 3]]),
+                                np.array([[0, 2, 4]]), np.array([2]), tids, np.array([2]), np.array([4]),
+                                np.array([9, 6]), np.array([0, 1]))
+    assert np.isneginf(out[0]).nonzero()[0].tolist() == [3]  # row 0 ends in 8
+    assert np.isneginf(out[1]).nonzero()[0].tolist() == [4]  # row 1 ends in the draft 9

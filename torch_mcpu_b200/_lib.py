@@ -96,6 +96,9 @@ SIGNATURES = {
     "mcpu_vllm_bias": (c_int, [c_void_p, c_int, c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p, c_void_p,
                                c_int64, c_int64, c_void_p, c_void_p, c_int64, c_void_p, c_int64, c_int64, c_void_p,
                                c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p]),
+    "mcpu_vllm_bad_words": (c_int, [c_void_p, c_int, c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p,
+                                    c_int64, c_int64, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64,
+                                    c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
     "mcpu_vllm_bincount": (c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64,
                                    c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_void_p]),
     "mcpu_device_error": (c_int, [ctypes.POINTER(c_int), c_int]),

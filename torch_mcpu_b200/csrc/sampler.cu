@@ -13,6 +13,8 @@
 //                                 (penalties.cpp:187-246)
 //   vllm_bias_kernel              allowed-token mask, logit bias, min-length
 //                                 stop tokens (logit_bias.cpp:15-96)
+//   vllm_bad_words_kernel         -inf on the last id of each bad word whose
+//                                 prefix ends the sequence (bad_words.cpp:13-82)
 // In the first three, each row is split over a cluster of 8 CTAs (256
 // threads each): every CTA
 // streams its eighth of the row (16-byte loads, four in flight per thread,
@@ -427,6 +429,61 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
+// Bad words (bad_words.cpp:13-82): one CTA per token row, one thread per
+// bad word of the row's request.  A bad word is ids[off[w] .. off[w+1]);
+// when its prefix (all but the last id) equals the last tokens of the row's
+// sequence — the request's output tokens all_token_ids[q, prompt_len ..
+// total_len) followed by the row's drafts input_ids[t-pos .. t) — its last
+// id becomes -inf.  Threads that ban the same id store the same value.
+// Indexes that would leave their tensors set the error flag and skip the
+// word (or the row), where the reference reads out of bounds.
+constexpr int kBadWordThreads = 128;
+
+template <typename T>
+__global__ void __launch_bounds__(kBadWordThreads)
+    bad_words_kernel(T* logits, long long stride, long long vocab, const int32_t* idx, long long num_reqs,
+                     const int32_t* bw_ids, long long bw_ids_stride, long long bw_ids_cols, const int32_t* bw_off,
+                     long long bw_off_stride, long long bw_off_cols, const int32_t* n_bw, const int32_t* atids,
+                     long long atids_stride, long long max_seq, const int32_t* plen, const int32_t* tlen,
+                     const int32_t* input_ids, const int32_t* local_pos) {
+  const long long tok = blockIdx.x;
+  const int32_t req = idx[tok];
+  bool bad = req < 0 || req >= num_reqs;
+  const int32_t nw = bad ? 0 : n_bw[req];
+  if (!bad && nw <= 0) return;
+  const int32_t pos = local_pos[tok];
+  const long long first = tok - pos;  // the request's first row in this batch
+  const int32_t pl = bad ? 0 : plen[req], tl = bad ? 0 : tlen[req];
+  bad = bad || pos < 0 || first < 0 || pl < 0 || tl < pl || tl > max_seq || nw + 1 > bw_off_cols;
+  if (bad) {
+    if (threadIdx.x == 0) atomicOr(&g_sampler_error, 1);
+    return;
+  }
+  const int32_t out_len = tl - pl;
+  const int32_t eff_len = out_len + pos;
+  const int32_t* off = bw_off + req * bw_off_stride;
+  const int32_t* ids = bw_ids + req * bw_ids_stride;
+  const int32_t* out = atids + req * atids_stride + pl;
+  T* row = logits + tok * stride;
+  for (int w = threadIdx.x; w < nw; w += kBadWordThreads) {
+    const int32_t start = off[w], end = off[w + 1];
+    const int32_t prefix = end - start - 1;
+    if (prefix > eff_len) continue;
+    if (end - 1 < 0 || end - 1 >= bw_ids_cols || (prefix > 0 && start < 0)) {
+      atomicOr(&g_sampler_error, 1);
+      continue;
+    }
+    bool match = true;
+    for (int32_t i = 0; i < prefix && match; ++i) {
+      const int32_t p = eff_len - prefix + i;  // position in output tokens + drafts
+      const int32_t actual = p >= out_len ? input_ids[first + (p - out_len)] : out[p];
+      match = ids[start + i] == actual;
+    }
+    const int32_t last = ids[end - 1];
+    if (match && last >= 0 && last < vocab) row[last] = neg_inf<T>();
+  }
+}
+
 orError_t check_float(int dtype, const char* op) {
   MCPU_ARG_CHECK(dtype == MCPU_FLOAT32 || dtype == MCPU_FLOAT16 || dtype == MCPU_BFLOAT16,
                  "%s: logits must be float32, float16 or bfloat16 (dtype code %d)", op, dtype);
@@ -623,4 +680,44 @@ extern "C" orError_t mcpu_vllm_bias(void* logits, int dtype, int64_t num_tokens,
     MCPU_BIAS(__nv_bfloat16);
 #undef MCPU_BIAS
   return from_cuda(cudaGetLastError(), "vllm_bias_kernel launch");
+}
+
+extern "C" orError_t mcpu_vllm_bad_words(void* logits, int dtype, int64_t num_tokens, int64_t logits_stride,
+                                         int64_t vocab_size, const int32_t* expanded_idx_mapping,
+                                         int64_t max_num_reqs, const int32_t* bad_word_token_ids,
+                                         int64_t bw_ids_stride, int64_t bw_ids_cols,
+                                         const int32_t* bad_word_offsets, int64_t bw_off_stride,
+                                         int64_t bw_off_cols, const int32_t* num_bad_words,
+                                         const int32_t* all_token_ids, int64_t token_ids_stride,
+                                         int64_t max_seq_len, const int32_t* prompt_len, const int32_t* total_len,
+                                         const int32_t* input_ids, const int32_t* expanded_local_pos,
+                                         orStream_t stream) {
+  orError_t e = sampler::check_float(dtype, "vllm_bad_words_kernel");
+  if (e != orSuccess) return e;
+  MCPU_ARG_CHECK(num_tokens >= 0 && num_tokens < (1LL << 31), "vllm_bad_words_kernel: bad num_tokens");
+  MCPU_ARG_CHECK(vocab_size > 0 && vocab_size <= logits_stride && vocab_size < (1LL << 31),
+                 "vllm_bad_words_kernel: vocab_size %lld out of range", static_cast<long long>(vocab_size));
+  MCPU_ARG_CHECK(bw_ids_cols >= 0 && bw_ids_cols <= bw_ids_stride && bw_off_cols >= 0 &&
+                     bw_off_cols <= bw_off_stride && max_seq_len >= 0 && max_seq_len <= token_ids_stride,
+                 "vllm_bad_words_kernel: widths exceed their strides");
+  if (num_tokens == 0) return orSuccess;
+  MCPU_ARG_CHECK(max_num_reqs > 0, "vllm_bad_words_kernel: no requests");
+  MCPU_ARG_CHECK(logits && expanded_idx_mapping && bad_word_token_ids && bad_word_offsets && num_bad_words &&
+                     all_token_ids && prompt_len && total_len && input_ids && expanded_local_pos,
+                 "vllm_bad_words_kernel: NULL pointer");
+  const dim3 grid(static_cast<unsigned>(num_tokens));
+  cudaStream_t st = as_cuda(stream);
+#define MCPU_BAD_WORDS(T)                                                                                        \
+  sampler::bad_words_kernel<T><<<grid, sampler::kBadWordThreads, 0, st>>>(                                       \
+      static_cast<T*>(logits), logits_stride, vocab_size, expanded_idx_mapping, max_num_reqs, bad_word_token_ids, \
+      bw_ids_stride, bw_ids_cols, bad_word_offsets, bw_off_stride, bw_off_cols, num_bad_words, all_token_ids,     \
+      token_ids_stride, max_seq_len, prompt_len, total_len, input_ids, expanded_local_pos)
+  if (dtype == MCPU_FLOAT32)
+    MCPU_BAD_WORDS(float);
+  else if (dtype == MCPU_FLOAT16)
+    MCPU_BAD_WORDS(__half);
+  else
+    MCPU_BAD_WORDS(__nv_bfloat16);
+#undef MCPU_BAD_WORDS
+  return from_cuda(cudaGetLastError(), "vllm_bad_words_kernel launch");
 }

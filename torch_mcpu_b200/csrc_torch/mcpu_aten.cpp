@@ -815,6 +815,47 @@ void vllm_bias_kernel(at::Tensor& logits, int64_t vocab_size, const at::Tensor& 
           "vllm_bias_kernel");
 }
 
+// csrc/aten/vllm_kernels/bad_words.cpp:84-180 (checks) and 184-198 (schema)
+void vllm_bad_words_kernel(at::Tensor& logits, const at::Tensor& expanded_idx_mapping,
+                           const at::Tensor& bad_word_token_ids, const at::Tensor& bad_word_offsets,
+                           const at::Tensor& num_bad_words, const at::Tensor& all_token_ids,
+                           const at::Tensor& prompt_len, const at::Tensor& total_len, const at::Tensor& input_ids,
+                           const at::Tensor& expanded_local_pos) {
+  TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "logits must be 2-D with unit column stride");
+  const int dt = sampler_dtype(logits, "logits");
+  auto int1d = [](const at::Tensor& t, const char* name) {
+    TORCH_CHECK(t.dim() == 1 && t.scalar_type() == at::kInt, name, " must be 1-D int32");
+    return t.contiguous();
+  };
+  auto int2d = [](const at::Tensor& t, const char* name) {
+    TORCH_CHECK(t.dim() == 2 && t.scalar_type() == at::kInt && t.stride(1) == 1, name,
+                " must be 2-D int32 with unit column stride");
+  };
+  const at::Tensor idx = int1d(expanded_idx_mapping, "expanded_idx_mapping");
+  const at::Tensor nbw = int1d(num_bad_words, "num_bad_words");
+  const at::Tensor pl = int1d(prompt_len, "prompt_len");
+  const at::Tensor tl = int1d(total_len, "total_len");
+  const at::Tensor inp = int1d(input_ids, "input_ids");
+  const at::Tensor lpos = int1d(expanded_local_pos, "expanded_local_pos");
+  int2d(bad_word_token_ids, "bad_word_token_ids");
+  int2d(bad_word_offsets, "bad_word_offsets");
+  int2d(all_token_ids, "all_token_ids");
+  const int64_t n = logits.size(0);
+  TORCH_CHECK(idx.numel() >= n && inp.numel() >= n && lpos.numel() >= n,
+              "vllm_bad_words_kernel: per-token tensors shorter than the rows");
+  const int64_t reqs = std::min({nbw.numel(), pl.numel(), tl.numel(), bad_word_token_ids.size(0),
+                                 bad_word_offsets.size(0), all_token_ids.size(0)});
+  MCPU_OK(mcpu_vllm_bad_words(logits.data_ptr(), dt, n, logits.stride(0), logits.size(1),
+                              idx.const_data_ptr<int32_t>(), reqs, bad_word_token_ids.const_data_ptr<int32_t>(),
+                              bad_word_token_ids.stride(0), bad_word_token_ids.size(1),
+                              bad_word_offsets.const_data_ptr<int32_t>(), bad_word_offsets.stride(0),
+                              bad_word_offsets.size(1), nbw.const_data_ptr<int32_t>(),
+                              all_token_ids.const_data_ptr<int32_t>(), all_token_ids.stride(0),
+                              all_token_ids.size(1), pl.const_data_ptr<int32_t>(), tl.const_data_ptr<int32_t>(),
+                              inp.const_data_ptr<int32_t>(), lpos.const_data_ptr<int32_t>(), stream_of(logits)),
+          "vllm_bad_words_kernel");
+}
+
 // Row-parallel down projection + SUM all-reduce of the partials in one kernel
 // (mm, csrc/aten/ops/mm.cpp:13-51, then McpuBackend::allreduce,
 // torch_mcpu/csrc/Distributed.cpp:403-413).  `window` is the address of the
@@ -925,6 +966,9 @@ TORCH_LIBRARY_FRAGMENT(mcpu, m) {
   m.def("vllm_bias_kernel(Tensor(a!) logits, int vocab_size, Tensor expanded_idx_mapping, "
         "Tensor num_allowed_token_ids, Tensor allowed_token_ids, Tensor num_logit_bias, Tensor bias_token_ids, "
         "Tensor bias, Tensor pos, Tensor min_lens, Tensor num_stop_token_ids, Tensor stop_token_ids) -> ()");
+  m.def("vllm_bad_words_kernel(Tensor(a!) logits, Tensor expanded_idx_mapping, Tensor bad_word_token_ids, "
+        "Tensor bad_word_offsets, Tensor num_bad_words, Tensor all_token_ids, Tensor prompt_len, "
+        "Tensor total_len, Tensor input_ids, Tensor expanded_local_pos) -> ()");
   m.def("vllm_bincount_kernel(Tensor expanded_idx_mapping, Tensor all_token_ids, Tensor prompt_len, "
         "Tensor prefill_len, Tensor(a!) prompt_bin_mask, Tensor(b!) output_bin_counts) -> ()");
   m.def("moe_align_block_size(Tensor topk_ids, int num_experts, int block_size, Tensor(a!) sorted_token_ids, "
@@ -945,5 +989,6 @@ TORCH_LIBRARY_IMPL(mcpu, PrivateUse1, m) {
   m.impl("vllm_penalties_kernel", vllm_penalties_kernel);
   m.impl("vllm_bincount_kernel", vllm_bincount_kernel);
   m.impl("vllm_bias_kernel", vllm_bias_kernel);
+  m.impl("vllm_bad_words_kernel", vllm_bad_words_kernel);
   m.impl("moe_align_block_size", moe_align_block_size);
 }
