@@ -2,14 +2,14 @@
 vllm_topk_log_softmax_kernel, vllm_ranks_kernel; csrc/aten/vllm_kernels/
 min_p.cpp, logprob.cpp; vllm_penalties_kernel, vllm_bincount_kernel:
 penalties.cpp; vllm_bias_kernel: logit_bias.cpp; vllm_bad_words_kernel:
-bad_words.cpp) on the B200 against the
-oracle, called as the reference's users call them (torch.ops.mcpu on mcpu tensors): fp32, fp16
-and bf16 logits, vocabularies with 16-byte-aligned and unaligned rows, a
-row stride wider than the vocabulary, -inf and NaN entries, p = 0 rows and
-out-of-range ids.  ranks are exact; log-probabilities within 2e-6; min_p
-results identical except where an entry lies within one fp32 ulp of the
-threshold (the threshold's logarithm is rounded once from fp64); penalties,
-bincount, bias and bad words bit-exact."""
+bad_words.cpp) on the B200 against the oracle, called as the reference's
+users call them (torch.ops.mcpu on mcpu tensors): fp32, fp16 and bf16
+logits, vocabularies with 16-byte-aligned and unaligned rows, a row stride
+wider than the vocabulary, -inf and NaN entries, p = 0 rows and out-of-range
+ids.  ranks are exact; log-probabilities within 2e-6; min_p results identical
+except where an entry lies within one fp32 ulp of the threshold (the
+threshold's logarithm is rounded once from fp64); penalties, bincount, bias
+and bad words bit-exact."""
 
 import numpy as np
 import pytest
