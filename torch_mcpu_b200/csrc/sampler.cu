@@ -260,6 +260,15 @@ constexpr int kPenElems = 8;
 constexpr int kPenChunk = kThreads * kPenElems;
 
 template <typename T>
+struct PenVec;  // four logits in one load
+template <>
+struct PenVec<float> { using type = float4; };
+template <>
+struct PenVec<__half> { using type = uint2; };
+template <>
+struct PenVec<__nv_bfloat16> { using type = uint2; };
+
+template <typename T>
 __global__ void __launch_bounds__(kThreads)
     penalties_kernel(T* logits, long long stride, long long vocab, const int32_t* idx, const int32_t* tids,
                      const int32_t* lpos, const float* rep, const float* freq, const float* pres,
@@ -284,41 +293,75 @@ __global__ void __launch_bounds__(kThreads)
   T* row = logits + tok * stride;
   const int32_t* orow = obc + req * obc_stride;
   const int32_t* prow = pbm + req * pbm_stride;
-  const long long v0 = static_cast<long long>(blockIdx.y) * kPenChunk + threadIdx.x;
+  const long long base = static_cast<long long>(blockIdx.y) * kPenChunk;
+  // With 16-byte-aligned logits and count rows, thread i takes the 4-element
+  // vectors i and i + 256 of the chunk (one 16-byte count load and one 16- or
+  // 8-byte logit load each); otherwise the elements i + 256 s, s < 8.
+  const bool vec = ((reinterpret_cast<uintptr_t>(row) | reinterpret_cast<uintptr_t>(orow)) & 15) == 0;
+  long long e[kPenElems];
+#pragma unroll
+  for (int s = 0; s < kPenElems; ++s)
+    e[s] = vec ? base + (static_cast<long long>((s / 4) * kThreads + threadIdx.x) << 2) + (s % 4)
+               : base + threadIdx.x + s * kThreads;
+  using Vec = typename PenVec<T>::type;
   int cnt[kPenElems];
   float x[kPenElems];
 #pragma unroll
-  for (int j = 0; j < kPenElems; ++j) {
-    const long long v = v0 + j * kThreads;
-    cnt[j] = v < vocab ? orow[v] : 0;
-    x[j] = v < vocab ? to_f(row[v]) : 0.0f;
+  for (int j = 0; j < kPenElems / 4; ++j) {
+    const long long e0 = e[j * 4];
+    if (vec && e0 + 3 < vocab) {
+      const int4 c = *reinterpret_cast<const int4*>(orow + e0);
+      const Vec u = *reinterpret_cast<const Vec*>(row + e0);
+      const T* t = reinterpret_cast<const T*>(&u);
+      cnt[j * 4] = c.x, cnt[j * 4 + 1] = c.y, cnt[j * 4 + 2] = c.z, cnt[j * 4 + 3] = c.w;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) x[j * 4 + k] = to_f(t[k]);
+    } else {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const long long v = e[j * 4 + k];
+        cnt[j * 4 + k] = v < vocab ? orow[v] : 0;
+        x[j * 4 + k] = v < vocab ? to_f(row[v]) : 0.0f;
+      }
+    }
   }
   if (use_drafts) {
-    for (int base = 0; base < pos; base += kThreads) {
-      const int nd = min(kThreads, pos - base);
+    for (int b0 = 0; b0 < pos; b0 += kThreads) {
+      const int nd = min(kThreads, pos - b0);
       __syncthreads();
-      if (static_cast<int>(threadIdx.x) < nd) drafts[threadIdx.x] = tids[d0 + base + threadIdx.x];
+      if (static_cast<int>(threadIdx.x) < nd) drafts[threadIdx.x] = tids[d0 + b0 + threadIdx.x];
       __syncthreads();
       for (int d = 0; d < nd; ++d) {
         const long long t = drafts[d];
 #pragma unroll
-        for (int j = 0; j < kPenElems; ++j) cnt[j] += t == v0 + j * kThreads ? 1 : 0;
+        for (int s = 0; s < kPenElems; ++s) cnt[s] += t == e[s] ? 1 : 0;
       }
     }
   }
+  alignas(16) T y[kPenElems];  // stored as whole vectors below
 #pragma unroll
-  for (int j = 0; j < kPenElems; ++j) {
-    const long long v = v0 + j * kThreads;
-    if (v >= vocab) continue;
-    float l = x[j];
-    const bool in_out = cnt[j] > 0;
-    if (rp != 1.0f) {
+  for (int s = 0; s < kPenElems; ++s) {
+    const long long v = e[s];
+    float l = x[s];
+    const bool in_out = cnt[s] > 0;
+    if (rp != 1.0f && v < vocab) {
       const bool in_prompt = (static_cast<uint32_t>(prow[v >> 5]) >> (v & 31)) & 1u;
       if (in_prompt || in_out) l = l > 0.0f ? __fdiv_rn(l, rp) : __fmul_rn(l, rp);
     }
-    l = __fsub_rn(l, __fmul_rn(fp, __int2float_rn(cnt[j])));
+    l = __fsub_rn(l, __fmul_rn(fp, __int2float_rn(cnt[s])));
     l = __fsub_rn(l, __fmul_rn(pp, in_out ? 1.0f : 0.0f));
-    row[v] = from_f<T>(l);
+    y[s] = from_f<T>(l);
+  }
+#pragma unroll
+  for (int j = 0; j < kPenElems / 4; ++j) {
+    const long long e0 = e[j * 4];
+    if (vec && e0 + 3 < vocab) {
+      *reinterpret_cast<Vec*>(row + e0) = *reinterpret_cast<const Vec*>(&y[j * 4]);
+    } else {
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        if (e[j * 4 + k] < vocab) row[e[j * 4 + k]] = y[j * 4 + k];
+    }
   }
 }
 
