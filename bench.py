@@ -332,7 +332,8 @@ def tp_mlp_leg(rank, world, pg, steps, warmup):
 
 def bandwidth_leg(dev, reps=20):
     """silu_and_mul on [8192, 2 x 18432] and rms_norm on [8192, 7168] (bf16,
-    the DeepSeek-V3 expert and hidden widths): CUDA-event time per call over rotating inputs
+    DeepSeek-V3 dense-MLP intermediate and hidden widths): CUDA-event time
+    per call over rotating inputs
     larger than L2, achieved GB/s of the algorithmic bytes."""
     import torch
 
