@@ -251,9 +251,13 @@ OPENREG_EXPORT orError_t mcpu_moe_align_workspace_bytes(int64_t numel, int num_e
  * orErrorInvalidValue and a message naming the limit.  It allocates nothing
  * and calls no allocating routine.  The first call on each device looks up
  * the array's device address (cudaGetSymbolAddress) on the current device;
- * make that first call before any stream capture.  All calls share the
- * array: calls whose kernels overlap on the GPU race, so order them on one
- * stream.  No counterpart in the reference.
+ * CUDA loads a library's device code lazily, so that first call is also the
+ * moment the 256 KiB array is placed in the device's memory: make it before
+ * the caller reserves its memory pool, and before any stream capture.  The
+ * address is kept per device for the life of the process; after a reset of
+ * the device's primary context, make a first call again in a fresh process.
+ * All calls share the array: calls whose kernels overlap on the GPU race,
+ * so order them on one stream.  No counterpart in the reference.
  */
 OPENREG_EXPORT orError_t mcpu_moe_align_block_size_static(const int32_t* topk_ids, int64_t numel, int num_experts,
                                                           int block_size, int32_t* sorted_token_ids,

@@ -208,6 +208,37 @@ def test_bias(mcpu, dtype, width, vocab):
     assert int(torch.isfinite(got[2, :vocab].float()).sum()) <= 512  # the allowed list keeps at most 512
 
 
+def test_bias_lists_read_with_their_own_row_strides(mcpu):
+    """bias_token_ids and bias with different row strides (views into wider
+    buffers): each list is read with its own tensor's row stride.  The
+    reference indexes the bias values with bias_token_ids.stride(0)
+    (logit_bias.cpp:65-66), the same row only when both strides agree, as they
+    do for the contiguous [max_num_reqs, max_bias] tensors vLLM passes."""
+    vocab, reqs = 32000, 4
+    g = torch.Generator().manual_seed(8)
+    na = torch.zeros(reqs, dtype=torch.int32)
+    allowed = torch.zeros(reqs, 8, dtype=torch.int32)
+    nb = torch.tensor([3, 0, 5, 2], dtype=torch.int32)
+    ids_wide = torch.randint(0, vocab, (reqs, 24), generator=g, dtype=torch.int32)
+    bias_wide = (0.5 * torch.randn(reqs, 40, generator=g)).float()
+    ml = torch.zeros(reqs, dtype=torch.int32)
+    ns = torch.zeros(reqs, dtype=torch.int32)
+    stop = torch.zeros(reqs, 2, dtype=torch.int32)
+    idx = torch.tensor([0, 1, 2, 3, 2, 0], dtype=torch.int32)
+    pos = torch.zeros(idx.numel(), dtype=torch.int64)
+    x = _logits(idx.numel(), vocab, torch.float32, 9)
+    xm = x.to("mcpu")
+    m = lambda t: t.to("mcpu")  # noqa: E731
+    ids_v, bias_v = m(ids_wide)[:, :16], m(bias_wide)[:, :16]
+    assert ids_v.stride(0) == 24 and bias_v.stride(0) == 40
+    torch.ops.mcpu.vllm_bias_kernel(xm, vocab, m(idx), m(na), m(allowed), m(nb), ids_v, bias_v, m(pos), m(ml),
+                                    m(ns), m(stop))
+    want = oracle.vllm_bias(x.numpy(), vocab, idx.numpy(), na.numpy(), allowed.numpy(), nb.numpy(),
+                            ids_wide[:, :16].numpy(), bias_wide[:, :16].numpy(), pos.numpy(), ml.numpy(),
+                            ns.numpy(), stop.numpy())
+    assert torch.equal(xm.cpu().view(torch.int32), torch.from_numpy(want).view(torch.int32))
+
+
 @pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("width,vocab", [(32000, 32000), (50016, 50000)])
 def test_bad_words(mcpu, dtype, width, vocab):

@@ -61,12 +61,29 @@ def test_static_scratch_entry_point_matches_the_workspace_one_on_two_calls():
     # router-sized call (65536 tokens, top-8 of 256 experts, block 64), then a
     # smaller one with another expert count: the second call reuses the array
     cases = [(g.integers(0, 256, (65536, 8)), 256, 64), (g.integers(0, 160, (1000, 6)), 160, 16)]
+    _check_cases(lib, stream, cases)
+
+
+def _check_cases(lib, stream, cases):
     for ids_np, E, bs in cases:
         ids = torch.from_numpy(ids_np.astype(np.int32)).cuda()
         want = _with_workspace(lib, ids, E, bs, stream)
         got = _static(lib, ids, E, bs, stream)
         for a, b in zip(got, want):
             assert torch.equal(a, b)
+
+
+def test_static_scratch_entry_point_at_its_limit_and_after_a_larger_matrix():
+    """Exactly at the limit (256 chunks x 256 experts = 65536 counters), then
+    a small call with 1024 experts whose count matrix is a different shape
+    than the counters the previous call left in the array."""
+    from torch_mcpu_b200 import _lib
+
+    lib = _lib.load()
+    stream = torch.cuda.current_stream().cuda_stream
+    g = np.random.default_rng(12)
+    cases = [(g.integers(0, 256, (4096 * 256,)), 256, 64), (g.integers(0, 1024, (3000, 8)), 1024, 32)]
+    _check_cases(lib, stream, cases)
 
 
 def test_static_scratch_entry_point_refuses_problems_beyond_its_limit():

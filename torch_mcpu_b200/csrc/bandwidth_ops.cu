@@ -300,11 +300,9 @@ static cudaError_t launch_rms_ring(void* out, const void* x, const void* w, int 
   int stages = (48 * 1024) / slot;
   stages = stages < 2 ? 2 : (stages > 4 ? 4 : stages);
   const int smem = stages * slot + stages * 8 + 2 * (kRmsThreads / 32) * 8 + 16;
-  static int configured = 0;
-  if (smem > 48 * 1024 && configured < smem) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (smem > 48 * 1024) {
+    cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), smem);
     if (e != cudaSuccess) return e;
-    configured = smem;
   }
   int per_sm = 1;
   cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kRmsThreads, smem);

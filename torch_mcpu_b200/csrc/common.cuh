@@ -17,6 +17,10 @@ void set_last_error(const char* fmt, ...);
 // Maps a CUDA status to orError_t, recording the CUDA message on failure.
 orError_t from_cuda(cudaError_t st, const char* what);
 
+// Raises `kernel`'s dynamic shared-memory limit to at least `bytes` on the
+// current device (once per kernel, device and size; thread-safe).
+cudaError_t ensure_dynamic_smem(const void* kernel, int bytes);
+
 // Driver entry point by name (cudaGetDriverEntryPoint), or nullptr.
 void* driver_entry(const char* name);
 

@@ -577,10 +577,8 @@ orError_t launch(const void* A, long long lda, const void* B, long long ldb, voi
   if (e != orSuccess) return e;
   e = make_map(&tb, B, N, K, ldb, BN);
   if (e != orSuccess) return e;
-  static std::once_flag attr_once;
-  std::call_once(attr_once, [] {
-    cudaFuncSetAttribute(gemm_bf16_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-  });
+  MCPU_CUDA_TRY(ensure_dynamic_smem(reinterpret_cast<const void*>(gemm_bf16_kernel<false>), SMEM_BYTES),
+                "mm shared-memory attribute");
   Params p;
   p.M = static_cast<int>(M);
   p.N = static_cast<int>(N);
@@ -627,10 +625,8 @@ orError_t launch_allreduce(const void* A, const void* B, long long M, long long 
   if (e != orSuccess) return e;
   e = make_map(&tb, B, N, K, K, BN);
   if (e != orSuccess) return e;
-  static std::once_flag attr_once;
-  std::call_once(attr_once, [] {
-    cudaFuncSetAttribute(gemm_bf16_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES_AR);
-  });
+  MCPU_CUDA_TRY(ensure_dynamic_smem(reinterpret_cast<const void*>(gemm_bf16_kernel<true>), SMEM_BYTES_AR),
+                "mm_allreduce shared-memory attribute");
   int per_sm = 0;
   MCPU_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemm_bf16_kernel<true>, THREADS_AR,
                                                               SMEM_BYTES_AR),

@@ -330,11 +330,9 @@ template <typename InT, int GS_MAX, bool kFast>
 static cudaError_t launch_tma_t(const Params& p, const CUtensorMap& tm, int tiles, int tpt, int smem,
                                 cudaStream_t st) {
   auto kern = grouped_topk_tma_kernel<InT, GS_MAX, kFast>;
-  static int configured_smem = 0;  // per instantiation
-  if (configured_smem < smem) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  {
+    cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), smem);
     if (e != cudaSuccess) return e;
-    configured_smem = smem;
   }
   int dev = 0, sms = 148, per_sm = 1;
   cudaGetDevice(&dev);
@@ -366,11 +364,9 @@ static int device_sms() {
 template <typename InT, int G, int GS_MAX, bool kFast>
 static cudaError_t launch_hot_t(const Params& p, const CUtensorMap& tm, int smem, cudaStream_t st) {
   auto kern = grouped_topk_hot_kernel<InT, G, GS_MAX, kFast>;
-  static int configured = 0;
-  if (configured < smem) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  {
+    cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), smem);
     if (e != cudaSuccess) return e;
-    configured = smem;
   }
   constexpr int TPT = kHotThreads / G;
   const long long tiles = (p.T + TPT - 1) / TPT;
@@ -386,11 +382,9 @@ static cudaError_t launch_hot_t(const Params& p, const CUtensorMap& tm, int smem
 template <int GS_MAX>
 static cudaError_t launch_quad_t(const Params& p, int smem, cudaStream_t st, EncodeTiledFn enc) {
   auto kern = grouped_topk_quad_kernel<GS_MAX>;
-  static int configured = 0;
-  if (configured < smem) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  {
+    cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), smem);
     if (e != cudaSuccess) return e;
-    configured = smem;
   }
   CUtensorMap tm;
   cuuint64_t gdim[2] = {static_cast<cuuint64_t>(p.E), static_cast<cuuint64_t>(p.T)};

@@ -240,13 +240,9 @@ orError_t launch(const int32_t* topk_ids, long long numel, int E, int bs, int32_
                  int32_t* expert_ids, long long eid_cap, int32_t* post_pad, int32_t* ws, int nchunks,
                  cudaStream_t st) {
   const int smem = (kWarps * E + E + 1 + 2 * kThreads) * 4;
-  static std::once_flag attr_once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(attr_once, [] {
-    attr_err = cudaFuncSetAttribute(align_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    (kWarps * kMaxExperts + kMaxExperts + 1 + 2 * kThreads) * 4);
-  });
-  MCPU_CUDA_TRY(attr_err, "moe_align_block_size scatter attribute");
+  MCPU_CUDA_TRY(ensure_dynamic_smem(reinterpret_cast<const void*>(align_scatter_kernel),
+                                   (kWarps * kMaxExperts + kMaxExperts + 1 + 2 * kThreads) * 4),
+                "moe_align_block_size scatter attribute");
   if (nchunks > 0) {
     align_count_kernel<<<nchunks, kThreads, 0, st>>>(topk_ids, numel, E, ws);
     MCPU_CUDA_TRY(cudaGetLastError(), "moe_align_block_size count launch");
@@ -331,7 +327,11 @@ static __device__ __align__(256) int32_t g_moe_static_counts[kStaticCounters];
 // Device address of the array on the current device.  In host code the
 // array's name is only a host-side stand-in, so the address is looked up
 // with cudaGetSymbolAddress once per device (on that device's first call)
-// and kept.
+// and kept.  With CUDA's lazy module loading that lookup is also what places
+// the array in the device's memory, so a caller that reserves all free
+// memory for its own pool makes its first call before reserving it.  The
+// kept address is that of the device's current primary context; a context
+// reset invalidates it.
 constexpr int kMaxDevices = 64;
 std::mutex g_static_mutex;
 int32_t* g_static_addr[kMaxDevices] = {};

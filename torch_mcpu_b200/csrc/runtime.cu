@@ -9,7 +9,10 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <map>
+#include <mutex>
 #include <thread>
+#include <utility>
 
 #include "common.cuh"
 
@@ -60,6 +63,23 @@ static orError_t poll_until(Query q, const char* what) {
     }
     if (spins > 64) std::this_thread::sleep_for(std::chrono::microseconds(20));
   }
+}
+
+cudaError_t ensure_dynamic_smem(const void* kernel, int bytes) {
+  // cudaFuncSetAttribute acts on the current device's context only, so the
+  // raised limit is recorded per (kernel, device); the map is shared by all
+  // host threads.
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, int> raised;
+  int dev = 0;
+  cudaError_t st = cudaGetDevice(&dev);
+  if (st != cudaSuccess) return st;
+  std::lock_guard<std::mutex> lock(mu);
+  int& have = raised[std::make_pair(kernel, dev)];
+  if (have >= bytes) return cudaSuccess;
+  st = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (st == cudaSuccess) have = bytes;
+  return st;
 }
 
 void* driver_entry(const char* name) {
