@@ -6,17 +6,22 @@ Workload (one "step"): the DeepSeek-V3-style grouped_topk router over one
 batch of 65536 tokens x 256 experts (fp32 logits N(0,1), fp32 bias N(0,0.01),
 8 groups, top-4 groups, top-8, sigmoid + bias, renormalised, x2.5).  Inputs
 rotate through 8 device buffers (8 x 67 MB > 2 x L2) so no step reads its
-logits from L2.  Steps are replayed from a CUDA graph of the C-ABI launches;
-W warm-up steps, then K timed steps between barriers and device syncs,
-timed with CUDA events on the launching stream, max over ranks.
+logits from L2.  W warm-up launches, then exactly K timed launches replayed
+from CUDA graphs of the C-ABI call, between barriers and device syncs, timed
+with CUDA events on the launching stream, max over ranks.
 
 Multi-GPU: the router is independent per token, so N ranks run N replicas
 (weak scaling, no collective on the data path); `value` is all ranks'
 tokens over the slowest rank's time.  The "tp_mlp" object reports the other
-half of the metric: the gated MLP H=4096 / I=14336 / T=2048 in bf16,
-tensor-parallel over the N ranks (TP=N), through the mcpu device (tcgen05
-GEMMs, fused SwiGLU) and its NCCL ProcessGroup (SUM all-reduce), in whole-job
-TFLOP/s over the slowest rank.
+half of the metric: the gated MLP of the TP example (H=4096 / I=14336 /
+T=2048) and the pre-rms_norm SwiGLU block (H=7168 / I=18432, T=8192 and
+T=256) in bf16, tensor-parallel over the N ranks (TP=N), through the mcpu
+device (tcgen05 GEMMs, fused SwiGLU) with the down projection and the SUM
+all-reduce fused over NVLink, the mm + NCCL form timed beside it; each case
+carries its TP=1 time on rank 0 of the same job and the scaling efficiency
+t_TP1 / (N t_N), and at N > 1 the fused all-reduce is checked bit for bit
+against the fp32 sum in rank order of the gathered partials (a mismatch
+fails the run).
 
 --impl reference times the reference algorithm on the host cores (the
 oracle's C restatement of the reference's CPU path, all threads), rank 0
@@ -51,15 +56,19 @@ GRAPH_STEPS = 64
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--steps", type=int, default=640)
     ap.add_argument("--warmup", type=int, default=64)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="bound on the host-core baseline's sampling time")
-    ap.add_argument("--legs", default="e2e,bw,moe,sampler,mlp,cpu",
-                    help="extra legs besides the router timing (comma list of e2e, bw, moe, sampler, mlp, cpu; "
-                         "'none' for the router alone, e.g. under a profiler)")
+    ap.add_argument("--legs", default="e2e,sweep,bw,moe,sampler,mlp,cpu",
+                    help="extra legs besides the router timing (comma list of e2e, sweep, bw, moe, sampler, mlp, "
+                         "cpu; 'none' for the router alone, e.g. under a profiler)")
+    ap.add_argument("--mlp-cases", default="M1,M2_T8192,M2_T256",
+                    help="tensor-parallel MLP cases of the mlp leg (comma list of M1, M2_T8192, M2_T256)")
     a = ap.parse_args()
+    if a.steps < 1 or a.warmup < 0:
+        ap.error("--steps must be >= 1 and --warmup >= 0")
     a.legs = set() if a.legs == "none" else set(a.legs.split(","))
     return a
 
@@ -98,7 +107,10 @@ def profiled_traffic(name: str):
 
 # ---------------------------------------------------------------- clocks
 class ClockSampler:
-    """Samples SM clock and clock-event reasons through NVML while running."""
+    """Samples the SM clock and the clock-event reasons through NVML, every
+    5 ms from __enter__ to __exit__, with the time of each sample so that a
+    summary can be given for a window (e.g. one timed region) as well as for
+    the whole device-busy span."""
 
     REASONS = {
         0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
@@ -108,8 +120,7 @@ class ClockSampler:
 
     def __init__(self, index: int):
         self.index = index
-        self.samples = []
-        self.reasons = 0
+        self.samples = []  # (monotonic time, SM MHz, reason bits)
         self._stop = threading.Event()
         self._t = None
         self.max_mhz = None
@@ -133,12 +144,12 @@ class ClockSampler:
         nv = self._nv
         while not self._stop.is_set():
             try:
-                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                mhz = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
                 try:
                     r = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
                 except AttributeError:
                     r = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self._h)
-                self.reasons |= int(r) & ~0x1
+                self.samples.append((time.monotonic(), mhz, int(r) & ~0x1))
             except Exception:
                 pass
             time.sleep(0.005)
@@ -148,13 +159,19 @@ class ClockSampler:
         if self._t:
             self._t.join()
 
-    def summary(self):
+    def summary(self, windows=None, what="the timed regions"):
+        sel = self.samples
+        if windows:
+            sel = [s for s in self.samples if any(a <= s[0] <= b for a, b in windows)]
+        reasons = 0
+        for s in sel:
+            reasons |= s[2]
         return {
-            "sm_mhz": statistics.median(self.samples) if self.samples else None,
+            "sm_mhz": statistics.median(s[1] for s in sel) if sel else None,
             "sm_max_mhz": self.max_mhz,
-            "samples": len(self.samples),
-            "reasons": [n for b, n in self.REASONS.items() if self.reasons & b],
-            "source": "nvml, 5 ms polling during the timed region",
+            "samples": len(sel),
+            "reasons": [n for b, n in self.REASONS.items() if reasons & b],
+            "source": f"nvml, 5 ms polling during {what}",
         }
 
 
@@ -264,70 +281,190 @@ def _graph_ms(step, pg, steps, warmup):
     return max_over_ranks(pg, e0.elapsed_time(e1)) / steps
 
 
-def tp_mlp_leg(rank, world, pg, steps, warmup):
-    """Gated MLP H=4096, I=14336, T=2048 (bf16), tensor-parallel over the
-    N ranks: fused gate/up GEMM + SwiGLU, then the row-parallel down
-    projection and the SUM all-reduce of the partials — at N > 1 as one
-    kernel over NVLink (mm_allreduce in a symmetric window), with the
-    mm + NCCL all-reduce form timed beside it.  Whole-job TFLOP/s over the
+def _bf16_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            pk = json.load(f)
+        return {"bf16_tflops": pk["bf16_tflops"], "bf16_tflops_sustained": pk["bf16_tflops_sustained"],
+                "kind": "measured"}
+    except Exception:
+        return {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "kind": "fallback"}
+
+
+MLP_CASES = {"M1": "MLP_M1", "M2_T8192": "MLP_M2_LARGE", "M2_T256": "MLP_M2_SMALL"}
+
+
+class _Shard:
+    """One rank's weights and buffers of a TP MLP case on the mcpu device."""
+
+    def __init__(self, cfg, tp, rank):
+        import torch
+
+        import configs as C
+        from torch_mcpu_b200 import ops
+
+        x, rms_w, wgu, wd = C.mlp_weights(cfg, tp, rank)
+        self.cfg = cfg
+        self.x = x.to("mcpu")
+        self.rms = None if rms_w is None else rms_w.to("mcpu")
+        self.wgu = ops.interleave_gate_up(wgu).to("mcpu")
+        self.wd = wd.to("mcpu")
+        self.normed = torch.empty(cfg.T, cfg.H, dtype=torch.bfloat16, device="mcpu") if cfg.pre_norm else None
+        self.act = torch.empty(cfg.T, wgu.size(0) // 2, dtype=torch.bfloat16, device="mcpu")
+        self.y = torch.empty(cfg.T, cfg.H, dtype=torch.bfloat16, device="mcpu")
+
+    def front(self):
+        """rms_norm (replicated) and the column-parallel gate/up GEMM + SwiGLU."""
+        import torch
+
+        import configs as C
+
+        h = self.x
+        if self.rms is not None:
+            torch.ops.mcpu.rms_norm(self.normed, self.x, self.rms, C.RMS_EPS)
+            h = self.normed
+        torch.ops.mcpu.gemm_swiglu.out(h, self.wgu, out=self.act)
+
+    def partial(self):
+        import torch
+
+        torch.mm(self.act, self.wd.t(), out=self.y)
+        return self.y
+
+
+def _check_fused(shard, win, world, pg):
+    """The fused down projection + all-reduce against the fp32 sum, in rank
+    order, of every rank's bf16 partial (gathered with NCCL), rounded once
+    to bf16: bit for bit on rank 0, and the same bits on every rank (digest
+    of each rank's output).  The NCCL all-reduce of the same partials is
+    compared too (its sum rounds at every step, so only within tolerance).
+    Raises on a mismatch."""
+    import hashlib
+
+    import torch
+    import torch.distributed as dist
+
+    from torch_mcpu_b200 import symm
+
+    shard.front()
+    part = shard.partial().clone()
+    gathered = torch.empty(world * part.size(0), part.size(1), dtype=part.dtype, device="mcpu")
+    dist.all_gather_into_tensor(gathered, part)
+    fused = symm.mm_allreduce(shard.act, shard.wd, win).clone()
+    nccl = part.clone()
+    dist.all_reduce(nccl)
+    torch.mcpu.synchronize()
+    fused_cpu = fused.cpu()
+    digest = hashlib.blake2b(fused_cpu.view(torch.int16).numpy().tobytes(), digest_size=16).hexdigest()
+    digests = [None] * world
+    dist.all_gather_object(digests, digest)
+    result = {"ranks_identical": len(set(digests)) == 1}
+    if pg is not None and dist.get_rank() == 0:
+        parts = gathered.cpu().view(world, part.size(0), part.size(1))
+        acc = parts[0].float()
+        for r in range(1, world):
+            acc = acc + parts[r].float()
+        want = acc.to(torch.bfloat16)
+        ndiff = int((fused_cpu.view(torch.int16) != want.view(torch.int16)).sum())
+        nccl_cpu = nccl.cpu().float()
+        rel = float((nccl_cpu - want.float()).norm() / want.float().norm().clamp_min(1e-30))
+        result.update({"fused_vs_fp32_rank_order_sum_differing_elements": ndiff,
+                       "nccl_vs_fp32_sum_rel_frobenius": rel})
+    ok = torch.tensor([0 if result["ranks_identical"] and result.get(
+        "fused_vs_fp32_rank_order_sum_differing_elements", 0) == 0 and result.get(
+        "nccl_vs_fp32_sum_rel_frobenius", 0.0) < 1e-2 else 1], dtype=torch.int32)
+    dist.all_reduce(ok, op=dist.ReduceOp.MAX)
+    if int(ok.item()) != 0:
+        raise SystemExit(f"bench: fused down projection + all-reduce check failed: {result}")
+    result["passed"] = True
+    return result
+
+
+def tp_case(name, rank, world, pg, steps, warmup, peaks):
+    """One TP MLP case at TP = N: the step (rms_norm if the block has one,
+    gate/up GEMM + SwiGLU, down projection + SUM all-reduce) replayed from a
+    CUDA graph, fused over NVLink at N > 1 with the mm + NCCL step timed
+    beside it; rank 0 also times the whole block at TP=1 on its own GPU
+    (the anchor of the scaling efficiency).  Whole-job TFLOP/s over the
     slowest rank's CUDA-event time."""
     import torch
 
     import configs as C
-
-    cfg = C.MLP_M1
-    x, _, wgu, wd = C.mlp_weights(cfg, world, rank)
     from torch_mcpu_b200 import ops, symm
 
-    xm = x.to("mcpu")
-    wgu_il = ops.interleave_gate_up(wgu).to("mcpu")
-    wdm = wd.to("mcpu")
-    act = torch.empty(cfg.T, wgu.size(0) // 2, dtype=torch.bfloat16, device="mcpu")
-    y = torch.empty(cfg.T, cfg.H, dtype=torch.bfloat16, device="mcpu")
+    cfg = getattr(C, MLP_CASES[name])
+    shard = _Shard(cfg, world, rank)
 
     def step_nccl():
-        torch.ops.mcpu.gemm_swiglu.out(xm, wgu_il, out=act)
-        torch.mm(act, wdm.t(), out=y)
+        shard.front()
+        y = shard.partial()
         if pg is not None:
             pg.all_reduce(y)
 
     nccl_ms = _graph_ms(step_nccl, pg, steps, warmup)
-    ms, mode = nccl_ms, "mm + all_reduce over the mcpu ProcessGroup (NCCL)" if world > 1 else "mm"
+    ms, mode, check = nccl_ms, "mm", None
     if world > 1:
         win = symm.SymmetricWindow(symm.window_bytes(cfg.T, cfg.H, world))
 
         def step_fused():
-            torch.ops.mcpu.gemm_swiglu.out(xm, wgu_il, out=act)
-            symm.mm_allreduce(act, wdm, win)
+            shard.front()
+            symm.mm_allreduce(shard.act, shard.wd, win)
 
         ms = _graph_ms(step_fused, pg, steps, warmup)
         mode = "down projection + all-reduce fused over NVLink (mm_allreduce, symmetric window)"
         torch.mcpu.synchronize()
         if ops.device_error():
-            raise RuntimeError("mm_allreduce: a bounded wait ran out during the TP leg")
+            raise SystemExit("bench: mm_allreduce: a bounded wait ran out during the TP leg")
+        check = _check_fused(shard, win, world, pg)
         win.close()
+    del shard
+    # TP=1 anchor: the whole block on rank 0's GPU alone, same job
+    tp1_ms = ms
+    if world > 1:
+        if rank == 0:
+            full = _Shard(cfg, 1, 0)
+
+            def step_one():
+                full.front()
+                full.partial()
+
+            tp1_ms = _graph_ms(step_one, None, steps, warmup)
+            del full
+        barrier(pg)
+        t = torch.tensor([tp1_ms], dtype=torch.float64)
+        pg.broadcast(t, src=0)
+        tp1_ms = float(t.item())
     flops = 2 * cfg.T * cfg.H * cfg.I * 3
-    peaks = {}
-    try:
-        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
-            pk = json.load(f)
-        peaks = {"bf16_tflops": pk["bf16_tflops"], "bf16_tflops_sustained": pk["bf16_tflops_sustained"]}
-    except Exception:
-        peaks = {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "kind": "fallback"}
     whole = flops / (ms * 1e-3) / 1e12
     per_gpu = whole / world
-    return {
-        "config": f"gated MLP bf16 H={cfg.H} I={cfg.I} T={cfg.T} TP={world} (gate/up column-parallel, "
-                  f"down row-parallel; {mode}; step replayed from a CUDA graph)",
+    out = {
+        "config": f"{'pre-rms_norm + ' if cfg.pre_norm else ''}SwiGLU MLP bf16 H={cfg.H} I={cfg.I} T={cfg.T} "
+                  f"TP={world} (gate/up column-parallel, down row-parallel; {mode}; step replayed from a CUDA graph)",
+        "ms_per_step": round(ms, 4),
         "nccl_ms_per_step": round(nccl_ms, 4),
+        "tp1_ms": round(tp1_ms, 4),
+        "scaling_efficiency": round(tp1_ms / (world * ms), 4),
         "tflops": round(whole, 1),
         "per_gpu_tflops": round(per_gpu, 1),
-        "ms_per_step": round(ms, 4),
         "frac_of_bf16_peak": round(per_gpu / peaks["bf16_tflops"], 4),
         "frac_of_bf16_sustained": round(per_gpu / peaks["bf16_tflops_sustained"], 4),
+        "peak_kind": peaks["kind"],
         "steps": steps,
         "flops_per_step": flops,
     }
+    if cfg.T <= 256:
+        # small-batch step: the weights' bytes bound it as much as the FLOPs
+        wbytes = 3 * cfg.H * cfg.I * 2 // world
+        out["weight_bytes_per_gpu"] = wbytes
+        out["weight_gbs_per_gpu"] = round(wbytes / (ms * 1e-3) / 1e9, 1)
+    if check is not None:
+        out["fused_check"] = check
+    return out
+
+
+def tp_mlp_leg(rank, world, pg, steps, warmup, cases):
+    peaks = _bf16_peaks()
+    return {name: tp_case(name, rank, world, pg, steps, warmup, peaks) for name in cases}
 
 
 def bandwidth_leg(dev, reps=20):
@@ -490,6 +627,100 @@ def sampler_leg(dev, reps=20):
 
 
 # ---------------------------------------------------------------- ours
+def _replay_plan(n, per_graph=GRAPH_STEPS):
+    """Exactly n launches as full graphs of per_graph launches plus one
+    remainder graph: (full replays, remainder size)."""
+    g = min(per_graph, n)
+    return g, n // g, n % g
+
+
+def router_sweep_leg(lib, dev, stream, reps=20):
+    """Latency per call at small batches (graph replay of 64 launches, inputs
+    resident) for the DeepSeek-V3 router at T in {1, 16, 256, 4096}, and the
+    softmax variant (160 experts, 8 groups, top-3 groups, top-6, no bias) at
+    65536 tokens over rotating inputs larger than L2, with its roofline at
+    160 x 4 + 6 x 8 = 688 algorithmic bytes per token."""
+    import torch
+
+    import configs as C
+
+    peak, peak_kind = measured_peaks()
+    out = {"latency_us": {}}
+
+    def timed(launch, n_in, per_graph=64):
+        with torch.cuda.stream(stream):
+            for i in range(3):
+                launch(i)
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(per_graph):
+                launch(i)
+        with torch.cuda.stream(stream):
+            graph.replay()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(reps):
+                graph.replay()
+            e1.record(stream)
+        e1.synchronize()
+        del graph
+        return e0.elapsed_time(e1) * 1e3 / (reps * per_graph)
+
+    for t in (1, 16, 256, 4096):
+        cfg = C.deepseek_v3(t)
+        gating, bias = C.router_inputs(cfg)
+        g, b = gating.to(dev), bias.to(dev)
+        w = torch.empty(t, K, dtype=torch.float32, device=dev)
+        ids = torch.empty(t, K, dtype=torch.int32, device=dev)
+
+        def launch(i, g=g, b=b, w=w, ids=ids, t=t):
+            rc = lib.mcpu_grouped_topk(g.data_ptr(), 0, t, E, G, TG, K, 1, 2.5, b.data_ptr(), 1, w.data_ptr(),
+                                       ids.data_ptr(), stream.cuda_stream)
+            if rc != 0:
+                from torch_mcpu_b200 import _lib
+
+                _lib.check(rc, "grouped_topk")
+
+        out["latency_us"][f"T{t}"] = round(timed(launch, 1), 2)
+    out["latency_config"] = "sigmoid+bias E=256 G=8 topk_group=4 topk=8, us per call, graph replay of 64 calls"
+
+    # softmax variant, throughput at 65536 tokens
+    cfg = C.softmax160(T)
+    E2, K2 = cfg.E, cfg.K
+    gating, _ = C.router_inputs(cfg)
+    bufs = [gating.to(dev)]
+    for i in range(1, N_BUFFERS):
+        gg = torch.Generator(device=dev).manual_seed(200 + i)
+        bufs.append(torch.randn(T, E2, generator=gg, device=dev))
+    w = torch.empty(T, K2, dtype=torch.float32, device=dev)
+    ids = torch.empty(T, K2, dtype=torch.int32, device=dev)
+
+    def launch_sm(i):
+        rc = lib.mcpu_grouped_topk(bufs[i % N_BUFFERS].data_ptr(), 0, T, E2, cfg.G, cfg.TG, K2, 0, 1.0, None, 0,
+                                   w.data_ptr(), ids.data_ptr(), stream.cuda_stream)
+        if rc != 0:
+            from torch_mcpu_b200 import _lib
+
+            _lib.check(rc, "grouped_topk")
+
+    us = timed(launch_sm, N_BUFFERS)
+    nbytes = T * (E2 * 4 + K2 * 8)
+    gbs = nbytes / (us * 1e-6) / 1e9
+    out["softmax160"] = {
+        "config": f"softmax E={E2} G={cfg.G} topk_group={cfg.TG} topk={K2}, no bias, T={T}, "
+                  f"{N_BUFFERS} rotating {T * E2 * 4 / 1e6:.1f} MB inputs",
+        "us_per_call": round(us, 2),
+        "mtok_s": round(T / (us * 1e-6) / 1e6, 1),
+        "algorithmic_bytes": nbytes,
+        "achieved_gbs": round(gbs, 1),
+        "peak_gbs": peak,
+        "frac": round(gbs / peak, 4),
+        "peak_kind": peak_kind,
+    }
+    return out
+
+
 def run_ours(a):
     import numpy as np
     import torch
@@ -532,42 +763,53 @@ def run_ours(a):
         if not np.array_equal(got, np.sort(oids, 1)):
             raise SystemExit("bench: router output differs from the oracle; refusing to time it")
 
-    # CUDA graph of GRAPH_STEPS launches (rotating buffers)
+    # exactly K timed launches: full graphs of up to GRAPH_STEPS launches plus
+    # a remainder graph, rotating over the input buffers
+    per, full, rem = _replay_plan(a.steps)
     graph = torch.cuda.CUDAGraph()
+    graph_rem = torch.cuda.CUDAGraph() if rem else None
     with torch.cuda.stream(stream):
         for i in range(3):
             launch(i)
     stream.synchronize()
     with torch.cuda.graph(graph, stream=stream):
-        for i in range(GRAPH_STEPS):
+        for i in range(per):
             launch(i)
-    reps_w = max(1, -(-a.warmup // GRAPH_STEPS))
-    reps = max(1, -(-a.steps // GRAPH_STEPS))
-    steps = reps * GRAPH_STEPS
+    if graph_rem is not None:
+        with torch.cuda.graph(graph_rem, stream=stream):
+            for i in range(rem):
+                launch(per + i)
+    steps = full * per + rem
 
     exact_before = ctypes.c_ulonglong(0)
     lib.mcpu_grouped_topk_exact_rows(ctypes.byref(exact_before), 1)
+    busy = []  # (start, end) of every timed region, for the clock record
+    clk = ClockSampler(local).__enter__()
     with torch.cuda.stream(stream):
-        for _ in range(reps_w):
-            graph.replay()
+        for i in range(a.warmup):
+            launch(i)
     stream.synchronize()
     barrier(pg)
     torch.cuda.synchronize(dev)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
-        with torch.cuda.stream(stream):
-            ev0.record(stream)
-            for _ in range(reps):
-                graph.replay()
-            ev1.record(stream)
-        ev1.synchronize()
+    t0 = time.monotonic()
+    with torch.cuda.stream(stream):
+        ev0.record(stream)
+        for _ in range(full):
+            graph.replay()
+        if graph_rem is not None:
+            graph_rem.replay()
+        ev1.record(stream)
+    ev1.synchronize()
     torch.cuda.synchronize(dev)
+    busy.append((t0, time.monotonic()))
     barrier(pg)
     ms = ev0.elapsed_time(ev1)
     ms_max = max_over_ranks(pg, ms)
     exact = ctypes.c_ulonglong(0)
     lib.mcpu_grouped_topk_exact_rows(ctypes.byref(exact), 0)
-    exact_per_step = exact.value / (steps + reps_w * GRAPH_STEPS)
+    exact_per_step = exact.value / (steps + a.warmup)
+    del graph, graph_rem
 
     # e2e through the C-ABI with host buffers: every step copies its logits
     # host -> device, routes them and copies its weights and ids back.  Two
@@ -609,38 +851,55 @@ def run_ours(a):
         used[b] = True
 
     e2e_ms = None
+    e2e_steps = max(3, min(a.steps, 200))
     if "e2e" in a.legs:
-        e2e_steps = max(3, min(a.steps, 200))
         for i in range(4):
             e2e_step(i)
         torch.cuda.synchronize(dev)
         barrier(pg)
+        t0 = time.monotonic()
         ev0.record(s_in)
         for i in range(e2e_steps):
             e2e_step(i)
         ev1.record(s_out)
         ev1.synchronize()
         torch.cuda.synchronize(dev)
+        busy.append((t0, time.monotonic()))
         barrier(pg)
         e2e_ms = max_over_ranks(pg, ev0.elapsed_time(ev1)) / e2e_steps
-    del graph
-    bw = bandwidth_leg(dev) if "bw" in a.legs else None
-    moe = moe_leg(dev, ids, stream) if "moe" in a.legs else None
-    sampler = sampler_leg(dev) if "sampler" in a.legs else None
-    mlp = tp_mlp_leg(rank, world, pg, steps=max(10, min(a.steps, 50)), warmup=3) if "mlp" in a.legs else None
+
+    def leg(name, fn):
+        t0 = time.monotonic()
+        r = fn()
+        busy.append((t0, time.monotonic()))
+        return r
+
+    sweep = leg("sweep", lambda: router_sweep_leg(lib, dev, stream)) if "sweep" in a.legs else None
+    bw = leg("bw", lambda: bandwidth_leg(dev)) if "bw" in a.legs else None
+    moe = leg("moe", lambda: moe_leg(dev, ids, stream)) if "moe" in a.legs else None
+    sampler = leg("sampler", lambda: sampler_leg(dev)) if "sampler" in a.legs else None
+    mlp = None
+    if "mlp" in a.legs:
+        cases = [c for c in a.mlp_cases.split(",") if c]
+        mlp = leg("mlp", lambda: tp_mlp_leg(rank, world, pg, steps=max(10, min(a.steps, 50)), warmup=3,
+                                            cases=cases))
+    clk.__exit__(None, None, None)
 
     if rank == 0:
         per_step = ms_max / steps
         peak, peak_kind = measured_peaks()
         achieved = BYTES_PER_TOKEN * T / (per_step * 1e-3) / 1e9
         traffic = profiled_traffic("grouped_topk_T65536_E256.md")
+        clocks = clk.summary(busy, "the timed regions of every leg (router, e2e, sweep, bandwidth, "
+                                   "dispatch, sampler and MLP legs)")
+        clocks["router_timed_region"] = clk.summary(busy[:1], "the router's timed region")
         line = {
             "metric": METRIC,
             "value": round(T * world / (per_step * 1e-3) / 1e6, 2),
             "unit": "Mtok/s",
             "n_gpus": world,
             "steps": steps,
-            "warmup": reps_w * GRAPH_STEPS,
+            "warmup": a.warmup,
             "ms_per_step": round(per_step, 6),
             "higher_is_better": True,
             "scaling": "weak",
@@ -663,13 +922,15 @@ def run_ours(a):
                 "unit": "Mtok/s",
                 "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h,
+                "steps": e2e_steps,
                 "path": "per step: orMemcpyAsync H2D (pinned) -> mcpu_grouped_topk -> orMemcpyAsync D2H (pinned); "
                         "two buffer sets on copy-in / router / copy-out streams, so step i+1's input copy "
                         "overlaps step i's router",
             },
-            "clocks": clk.summary(),
+            "clocks": clocks,
             "gpu_launches": steps,
             "exact_path_rows_per_step": round(exact_per_step, 2),
+            "router_sweep": sweep,
             "bandwidth_ops": bw,
             "moe_dispatch": moe,
             "sampler_ops": sampler,

@@ -8,6 +8,7 @@ device.  Standard deviations are read as std (N(0, 0.01) -> std 0.01).
 
 from __future__ import annotations
 
+import functools
 from dataclasses import dataclass
 
 import torch
@@ -138,7 +139,10 @@ def mlp_weights(cfg: MlpCfg, tp: int, rank: int):
     return x, rms_w, torch.cat([gate, up], 0), down_t.t().contiguous()
 
 
+@functools.lru_cache(maxsize=None)
 def _block_normal(seed: int, which: int, block: int, rows: int, cols: int) -> torch.Tensor:
+    """One fixed block of a weight matrix (cached: the TP degrees of one
+    configuration share their blocks, and torch.cat copies them out)."""
     g = torch.Generator().manual_seed((seed * 16 + which) * 64 + block)
     return (0.02 * torch.randn(rows, cols, generator=g, dtype=torch.float32)).to(torch.bfloat16)
 

@@ -1,9 +1,9 @@
 """Generate the golden fixtures in this folder from the reference itself.
 
-Run in a container that has the reference source at /root/reference (the
-fixtures are committed; the GPU tests never need the reference):
+Run where a checkout of the reference source is at hand (the fixtures are
+committed; the GPU tests never need the reference):
 
-    python tests/golden/gen_golden.py
+    python tests/golden/gen_golden.py --reference DIR   # or TORCH_MCPU_REFERENCE=DIR
 
 * grouped_topk: the reference's own router function ``copied_grouped_topk``
   (tests/test_grouped_topk_compile.py:15-66 of kzwrime/torch_mcpu) is loaded
@@ -39,10 +39,25 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, HERE)
 import configs as C  # noqa: E402
 
-REF_TEST = "/root/reference/tests/test_grouped_topk_compile.py"
+def _reference_test_file() -> str:
+    """tests/test_grouped_topk_compile.py of a kzwrime/torch_mcpu checkout
+    named by --reference DIR or the TORCH_MCPU_REFERENCE environment
+    variable."""
+    root = None
+    if "--reference" in sys.argv:
+        root = sys.argv[sys.argv.index("--reference") + 1]
+    root = root or os.environ.get("TORCH_MCPU_REFERENCE")
+    if not root:
+        raise SystemExit("gen_golden.py: give the reference checkout with --reference DIR "
+                         "or TORCH_MCPU_REFERENCE=DIR")
+    path = os.path.join(root, "tests", "test_grouped_topk_compile.py")
+    if not os.path.exists(path):
+        raise SystemExit(f"gen_golden.py: {path} not found")
+    return path
 
 
 def load_reference_router():
+    REF_TEST = _reference_test_file()
     src = open(REF_TEST).read()
     tree = ast.parse(src)
     fn = next(n for n in tree.body if isinstance(n, ast.FunctionDef) and n.name == "copied_grouped_topk")

@@ -99,3 +99,29 @@ def test_mm_rejects_bad_arguments():
         m.mm_nt(rand_bf16(16, 60), rand_bf16(32, 60))
     with pytest.raises(RuntimeError, match="bfloat16"):
         m.mm_nt(a.float(), rand_bf16(32, 64))
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_kernels_with_large_shared_memory_run_on_a_second_device_in_one_process():
+    """The raised shared-memory limit of a kernel belongs to one device's
+    context: a GEMM (over 48 KiB of shared memory), the MoE dispatch with
+    1024 experts and the router, first on device 0 and then on device 1 of
+    the same process, each against the same call on device 0."""
+    m = _m()
+    outs = []
+    g = torch.Generator().manual_seed(21)
+    a = (torch.randn(512, 256, generator=g)).to(torch.bfloat16)
+    b = (0.05 * torch.randn(384, 256, generator=g)).to(torch.bfloat16)
+    ids = torch.randint(0, 1024, (3000, 8), generator=g, dtype=torch.int32)
+    logits = torch.randn(300, 256, generator=g)
+    bias = 0.01 * torch.randn(256, generator=g)
+    for d in (0, 1):
+        dev = f"cuda:{d}"
+        with torch.cuda.device(d):
+            y = m.ops.mm_nt(a.to(dev), b.to(dev))
+            s, e, n = m.ops.moe_align_block_size(ids.to(dev), 32, 1024)
+            w, i = m.grouped_topk(logits.to(dev), logits.to(dev), 8, True, 8, 4, "sigmoid", 2.5, bias.to(dev))
+            torch.cuda.synchronize(d)
+            outs.append([t.cpu() for t in (y, s, e, n, w, i)])
+    for x0, x1 in zip(*outs):
+        assert torch.equal(x0, x1)

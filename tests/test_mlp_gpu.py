@@ -62,9 +62,15 @@ def test_mlp_matches_reference_fixture_and_oracle(name):
     assert rel(out.float().cpu().numpy(), oracle.bf16_bits_to_f32(ob)) < 2e-2
 
 
-@pytest.mark.parametrize("cfg,tp", [(C.MLP_M1, 1), (C.MLP_M1, 4), (C.MLP_M2_SMALL, 2)])
+@pytest.mark.parametrize("cfg,tp", [(C.MLP_M1, 1), (C.MLP_M1, 4)]
+                         + [(C.MLP_M2_LARGE, tp) for tp in (1, 2, 4, 8)]
+                         + [(C.MLP_M2_SMALL, tp) for tp in (1, 2, 4, 8)],
+                         ids=lambda v: v.name if isinstance(v, C.MlpCfg) else f"tp{v}")
 def test_mlp_full_shape_matches_fp32_pipeline(cfg, tp):
-    """Full weights; the fp32 reference is evaluated on 64 sampled rows."""
+    """Full weights at the benchmark shapes (the TP example's gated MLP, and
+    the pre-rms_norm SwiGLU block H=7168 / I=18432 at 8192 and 256 tokens),
+    every rank's shard run on one GPU and the partials summed; the fp32
+    reference is evaluated on 64 sampled rows."""
     from torch_mcpu_b200 import device_error
 
     device_error(reset=True)
