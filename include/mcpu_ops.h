@@ -266,6 +266,23 @@ OPENREG_EXPORT orError_t mcpu_moe_align_block_size_static(const int32_t* topk_id
                                                           int32_t* num_tokens_post_pad, orStream_t stream);
 
 /*
+ * The reference's stream test ops (csrc/aten/native/Extra.cpp:255-296,
+ * schemas mcpu::stream_sleep_fill_, stream_sleep_copy_, first_element_int),
+ * which make stream ordering observable:
+ *   mcpu_stream_sleep_fill_i64  on `stream`: wait sleep_ms (0..60000) on the
+ *     GPU's timer, then set the numel int64 values of x to `value`;
+ *   mcpu_stream_sleep_copy_i64  the same wait, then copy src into dst;
+ *   mcpu_read_i64_now           *out = *src (device memory), read at once
+ *     on a private stream: it does not wait for work queued on other
+ *     streams (the reference reads host memory directly).
+ */
+OPENREG_EXPORT orError_t mcpu_stream_sleep_fill_i64(int64_t* x, int64_t numel, int64_t value, int64_t sleep_ms,
+                                                    orStream_t stream);
+OPENREG_EXPORT orError_t mcpu_stream_sleep_copy_i64(int64_t* dst, const int64_t* src, int64_t numel,
+                                                    int64_t sleep_ms, orStream_t stream);
+OPENREG_EXPORT orError_t mcpu_read_i64_now(const int64_t* src, int64_t* out);
+
+/*
  * vLLM sampler kernels of the decode path, the reference's own mcpu ops
  * (csrc/aten/vllm_kernels/min_p.cpp, logprob.cpp; schemas
  * mcpu::vllm_min_p_kernel, vllm_topk_log_softmax_kernel, vllm_ranks_kernel).

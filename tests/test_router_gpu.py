@@ -139,6 +139,47 @@ def test_router_edge_configurations(cfg):
     _assert_parity(cfg, w, ids, ow, oids, oties, rtol)
 
 
+KERNEL_CASES = [C.deepseek_v3(t) for t in (1, 16, 33, 256, 1000, 4096, 65536)] + [
+    C.RouterCfg("TG2_K4", 777, 256, 8, 2, 4, "sigmoid", True, True, 1.0),
+    C.RouterCfg("TG3_K6_noscale", 515, 256, 8, 3, 6, "sigmoid", True, False, 2.5),
+    C.RouterCfg("TG4_K5", 300, 256, 8, 4, 5, "sigmoid", True, True, 2.5),
+    C.RouterCfg("TG1_K2", 64, 256, 8, 1, 2, "sigmoid", True, True, 1.0),
+]
+
+
+@pytest.mark.parametrize("kernel", ["pair", "quad"])
+@pytest.mark.parametrize("cfg", KERNEL_CASES, ids=lambda c: c.name)
+def test_router_pair_and_quad_kernels_at_every_size(cfg, kernel, monkeypatch):
+    """The DeepSeek-V3 shape (256 experts, 8 groups, fp32, sigmoid + bias) is
+    served by the pair kernel (two lanes per token) from 8192 tokens and by
+    the quad kernel (four lanes per token) below; each is forced here over
+    ragged, tiny and full-size batches and other topk_group / topk choices."""
+    monkeypatch.setenv("MCPU_ROUTER_KERNEL", kernel)
+    gating, bias = C.router_inputs(cfg)
+    w, ids = _gpu(cfg, gating, bias)
+    ow, oids, oties, _ = _oracle(cfg, gating, bias)
+    _assert_parity(cfg, w, ids, ow, oids, oties, 1e-6)
+
+
+@pytest.mark.parametrize("kernel", ["pair", "quad"])
+def test_router_many_equal_keys_take_the_exact_paths(kernel, monkeypatch):
+    """Rows whose keys tie in many places: all keys equal (every group and
+    expert margin is zero), and rows where a whole group ties, so the
+    candidate lists are long and both exact paths (group re-pick, exact
+    re-rank) run."""
+    monkeypatch.setenv("MCPU_ROUTER_KERNEL", kernel)
+    cfg = C.RouterCfg("ties_many", 96, 256, 8, 4, 8, "sigmoid", True, True, 2.5)
+    g = torch.Generator().manual_seed(4)
+    gating = torch.randn(96, 256, generator=g)
+    gating[0::3] = 0.0                      # every key equal
+    gating[1::3, 64:96] = 3.0               # group 2 ties at the top
+    gating[2::3, :] = torch.randn(1, 256, generator=g).round()  # coarse values, many equal keys
+    bias = torch.zeros(256)
+    w, ids = _gpu(cfg, gating, bias)
+    ow, oids, oties, _ = _oracle(cfg, gating, bias)
+    _assert_parity(cfg, w, ids, ow, oids, oties, 1e-6)
+
+
 def test_router_exact_ties_break_toward_lower_index():
     cfg = C.RouterCfg("ties", 40, 256, 8, 4, 8, "sigmoid", True, True, 2.5)
     gating = torch.zeros(40, 256)

@@ -26,6 +26,7 @@
 #include <cuda.h>
 #include <math.h>
 #include <stdlib.h>
+#include <string.h>
 
 #include "router_common.cuh"
 
@@ -316,6 +317,7 @@ __global__ void __launch_bounds__(kThreads) grouped_topk_kernel(const Params p) 
 #include "grouped_topk_tma.cuh"
 #include "grouped_topk_g8.cuh"
 #include "grouped_topk_quad.cuh"
+#include "grouped_topk_pair.cuh"
 
 
 namespace mcpu {
@@ -406,6 +408,47 @@ static cudaError_t launch_quad_t(const Params& p, int smem, cudaStream_t st, Enc
   return cudaGetLastError();
 }
 
+static cudaError_t launch_pair(const Params& p, cudaStream_t st, EncodeTiledFn enc) {
+  constexpr int NW = kPairWarps;
+  auto kern = grouped_topk_pair_kernel<NW>;
+  constexpr PairLayout L = pair_layout(NW);
+  {
+    cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), L.total);
+    if (e != cudaSuccess) return e;
+  }
+  CUtensorMap tm;
+  cuuint64_t gdim[2] = {static_cast<cuuint64_t>(kPairE), static_cast<cuuint64_t>(p.T)};
+  cuuint64_t gstride[1] = {static_cast<cuuint64_t>(kPairE) * 4};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(kPairGS), static_cast<cuuint32_t>(kPairTokens)};
+  cuuint32_t estr[2] = {1, 1};
+  if (enc(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(p.gating), gdim, gstride, box, estr,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return cudaErrorInvalidValue;
+  const long long wtiles = (p.T + kPairTokens - 1) / kPairTokens;
+  const long long ctas_needed = (wtiles + NW - 1) / NW;
+  const long long cap = device_sms();  // one CTA per SM
+  const int grid = static_cast<int>(ctas_needed < cap ? ctas_needed : cap);
+  const int vec_out = p.K == 8 && reinterpret_cast<uintptr_t>(p.w_out) % 16 == 0 &&
+                      reinterpret_cast<uintptr_t>(p.id_out) % 16 == 0;
+  kern<<<grid, NW * 32, L.total, st>>>(tm, p, wtiles, vec_out);
+  return cudaGetLastError();
+}
+
+// Tokens from which the pair kernel (two lanes per token) serves the
+// DeepSeek-V3 shape; below, the quad kernel (four lanes per token) spreads a
+// small batch over more warps.  MCPU_ROUTER_KERNEL=pair|quad forces a choice.
+constexpr long long kPairMinTokens = 8192;
+
+static bool use_pair_kernel(const Params& p) {
+  if (!(p.E == kPairE && p.G == kPairG && p.TG <= kPairTGMax && p.K <= kPairKMax && 2 * p.TG >= p.K)) return false;
+  if (p.T >= (1LL << 31) - kPairTokens) return false;
+  const char* force = getenv("MCPU_ROUTER_KERNEL");
+  if (force && strcmp(force, "pair") == 0) return true;
+  if (force && strcmp(force, "quad") == 0) return false;
+  return p.T >= kPairMinTokens;
+}
+
 // Which (segment width, group-size bound) the hot kernel is built for.
 template <typename InT, bool kFast>
 static bool dispatch_hot(const Params& p, const CUtensorMap& tm, int smem, cudaStream_t st,
@@ -441,6 +484,11 @@ static orError_t launch_hot(Params p, int dtype, bool fast, cudaStream_t st, boo
   static EncodeTiledFn enc = reinterpret_cast<EncodeTiledFn>(driver_entry("cuTensorMapEncodeTiled"));
   if (!enc) return orSuccess;
   if (!(p.G == 8 || (esz == 4 && (p.G == 4 || p.G == 16 || p.G == 32)))) return orSuccess;
+  // fp32 sigmoid + bias, 256 experts in 8 groups, large batches: the pair kernel
+  if (fast && use_pair_kernel(p)) {
+    *handled = true;
+    return from_cuda(launch_pair(p, st, enc), "grouped_topk launch");
+  }
   // fp32 sigmoid + bias with 8 groups: the quad kernel
   if (fast && p.G == 8 && p.GS % 4 == 0 && p.GS <= 32 && 2 * p.TG >= p.K && (p.T + 7) / 8 <= 0x0FFFFFFF) {
     cudaError_t err;

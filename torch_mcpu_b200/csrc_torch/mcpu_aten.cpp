@@ -945,7 +945,8 @@ TORCH_LIBRARY_IMPL(aten, PrivateUse1, m) {
 }
 
 // The reference's TORCH_LIBRARY(mcpu) block (csrc/aten/OpenRegExtra.cpp:
-// 147-162) owns the namespace; the hot-path ops join it as a fragment.
+// 147-162, registered in mcpu_extra.cpp) owns the namespace; the hot-path
+// ops join it as a fragment.
 TORCH_LIBRARY_FRAGMENT(mcpu, m) {
   m.def("grouped_topk(Tensor gating_output, int num_expert_group, int topk_group, int topk, "
         "bool renormalize, float routed_scaling_factor, Tensor? e_score_correction_bias, "
