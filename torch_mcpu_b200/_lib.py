@@ -86,6 +86,9 @@ SIGNATURES = {
     "mcpu_moe_align_workspace_bytes": (c_int, [c_int64, c_int, ctypes.POINTER(ctypes.c_uint64)]),
     "mcpu_moe_align_block_size_static": (c_int, [c_void_p, c_int64, c_int, c_int, c_void_p, c_int64, c_void_p,
                                                  c_int64, c_void_p, c_void_p]),
+    "mcpu_stream_sleep_fill_i64": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p]),
+    "mcpu_stream_sleep_copy_i64": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p]),
+    "mcpu_read_i64_now": (c_int, [c_void_p, c_void_p]),
     "mcpu_vllm_min_p": (c_int, [c_void_p, c_int, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_void_p]),
     "mcpu_vllm_topk_log_softmax": (c_int, [c_void_p, c_void_p, c_int, c_int64, c_int64, c_void_p, c_int64, c_int64,
                                            c_int64, c_void_p]),
