@@ -23,9 +23,11 @@ t_TP1 / (N t_N), and at N > 1 the fused all-reduce is checked bit for bit
 against the fp32 sum in rank order of the gathered partials (a mismatch
 fails the run).
 
---impl reference times the reference algorithm on the host cores (the
-oracle's C restatement of the reference's CPU path, all threads), rank 0
-only, on the same configuration.
+--impl reference times the reference's path on the host cores, rank 0
+only, on the same configuration: its router op chain (the ATen CPU kernels
+its mcpu ops run, in its order, with its single-threaded raw sigmoid loop)
+over the full batch per step, with silu_and_mul, rms_norm and the gated
+MLP step timed beside it (oracle/cpu_legs.py).
 
 Prints one JSON line (rank 0).
 """
@@ -59,7 +61,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=640)
     ap.add_argument("--warmup", type=int, default=64)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--cpu-seconds", type=float, default=12.0,
+    ap.add_argument("--cpu-seconds", type=float, default=6.0,
                     help="bound on the host-core baseline's sampling time")
     ap.add_argument("--legs", default="e2e,sweep,bw,moe,sampler,mlp,cpu",
                     help="extra legs besides the router timing (comma list of e2e, sweep, bw, moe, sampler, mlp, "
@@ -176,35 +178,40 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------- CPU leg
+def cpu_legs(seconds: float, steps=None, warmup=None, legs=None):
+    """The reference's path on the host cores (oracle/cpu_legs.py), in a
+    child process so that torch's intra-op threads are configured (passive
+    OpenMP waits) before torch loads."""
+    import subprocess
+
+    env = dict(os.environ)
+    env.setdefault("OMP_WAIT_POLICY", "PASSIVE")
+    env.pop("CUDA_VISIBLE_DEVICES", None)
+    cmd = [sys.executable, "-m", "oracle.cpu_legs", "--seconds", str(seconds)]
+    if steps is not None:
+        cmd += ["--steps", str(steps), "--warmup", str(warmup or 0)]
+    if legs:
+        cmd += ["--legs", legs]
+    r = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise SystemExit(f"bench: CPU legs failed:\n{r.stderr[-2000:]}")
+    return json.loads(r.stdout.strip().splitlines()[-1])
+
+
 def cpu_baseline(seconds: float):
-    """The reference algorithm on the host cores: the oracle's C restatement
-    of the reference's CPU path (kind "port"), all host threads."""
-    import numpy as np
-
-    import configs as C
-    import oracle
-
-    cfg = C.deepseek_v3(T)
-    gating, bias = C.router_inputs(cfg)
-    g, b = gating.numpy(), bias.numpy()
-    threads = os.cpu_count() or 1
-    oracle.grouped_topk(g[:1024], K, True, G, TG, "sigmoid", 2.5, b, nthreads=threads)
-    times = []
-    t_end = time.perf_counter() + seconds
-    while True:
-        t0 = time.perf_counter()
-        oracle.grouped_topk(g, K, True, G, TG, "sigmoid", 2.5, b, nthreads=threads)
-        times.append(time.perf_counter() - t0)
-        if time.perf_counter() > t_end or len(times) >= 200:
-            break
-    med = statistics.median(times)
+    """cpu_baseline of the line: the reference's router op chain on the full
+    batch (kind "port": a restatement of its mcpu path, the same ATen CPU
+    kernels in the same order with its single-threaded raw sigmoid loop),
+    with the other legs of the path beside it."""
+    legs = cpu_legs(seconds)
+    r = legs["router"]
     return {
-        "value": round(T / med / 1e6, 4),
+        "value": r["value"],
         "unit": "Mtok/s",
-        "cores": threads,
+        "cores": legs["host"]["torch_threads"],
         "kind": "port",
-        "sample": f"{len(times)} runs of the full {T}x{E} batch (median {med * 1e3:.1f} ms), "
-                  f"oracle C restatement with glibc expf, {threads} OpenMP threads",
+        "sample": r["sample"] + f"; host: {legs['host']['nproc']} x {legs['host']['cpu_model']}",
+        "legs": legs,
     }
 
 
@@ -943,20 +950,27 @@ def run_ours(a):
 
 
 def run_reference(a):
+    """The reference arm: the reference's router op chain on the host cores
+    (rank 0 only), K timed steps of the full batch after W warm-ups, with
+    the path's other legs timed within --cpu-seconds each."""
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
-    base = cpu_baseline(a.cpu_seconds)
+    legs = cpu_legs(a.cpu_seconds, steps=a.steps, warmup=a.warmup)
+    r = legs["router"]
+    host = legs["host"]
+    base = {"value": r["value"], "unit": "Mtok/s", "cores": host["torch_threads"], "kind": "port",
+            "sample": r["sample"] + f"; host: {host['nproc']} x {host['cpu_model']}"}
     line = {
         "impl": "reference",
         "metric": METRIC,
-        "value": base["value"],
+        "value": r["value"],
         "unit": "Mtok/s",
         "n_gpus": world,
         "steps": a.steps,
         "warmup": a.warmup,
-        "ms_per_step": round(T / (base["value"] * 1e6) * 1e3, 3),
+        "ms_per_step": r["ms_per_batch"],
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
@@ -964,8 +978,8 @@ def run_reference(a):
         "data": "synthetic (seeded N(0,1) logits, N(0,0.01) bias)",
         "config": workload_config(1),
         "cpu_baseline": base,
-        "e2e": {"value": base["value"], "unit": "Mtok/s", "h2d_bytes_per_step": 0,
-                "d2h_bytes_per_step": 0},
+        "e2e": {"value": r["value"], "unit": "Mtok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "cpu_legs": legs,
     }
     print(json.dumps(line), flush=True)
 

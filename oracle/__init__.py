@@ -57,6 +57,8 @@ def _load():
     lib.oracle_rms_norm_bf16.restype = ctypes.c_int
     lib.oracle_sigmoid_f32.argtypes = [P, ctypes.c_int64, P, ctypes.c_int]
     lib.oracle_sigmoid_f32.restype = None
+    lib.oracle_silu_raw_bf16.argtypes = [P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, P, ctypes.c_int]
+    lib.oracle_silu_raw_bf16.restype = None
     _lib = lib
     return lib
 
@@ -138,6 +140,17 @@ def sigmoid_f32(x: np.ndarray, exp_mode: int = EXP_GLIBC) -> np.ndarray:
     x = np.ascontiguousarray(x, dtype=np.float32)
     out = np.empty_like(x)
     lib.oracle_sigmoid_f32(_ptr(x), x.size, _ptr(out), exp_mode)
+    return out
+
+
+def silu_raw_bf16(x_bits: np.ndarray, d: int, exp_mode: int = EXP_GLIBC) -> np.ndarray:
+    """The reference's single-threaded raw silu loop on the first d columns
+    of x (bf16 bits [T, pitch]) -> bf16 bits [T, d]."""
+    lib = _load()
+    x = np.ascontiguousarray(x_bits, dtype=np.uint16)
+    T, pitch = x.shape
+    out = np.empty((T, d), np.uint16)
+    lib.oracle_silu_raw_bf16(_ptr(x), T, d, pitch, _ptr(out), exp_mode)
     return out
 
 

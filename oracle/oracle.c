@@ -331,3 +331,14 @@ int oracle_rms_norm_bf16(const uint16_t* x, const uint16_t* w, int64_t T,
 void oracle_sigmoid_f32(const float* x, int64_t n, float* out, int exp_mode) {
   for (int64_t i = 0; i < n; ++i) out[i] = sigmoid_f(x[i], exp_mode);
 }
+
+/* The reference's raw silu loop on bf16 (csrc/aten/ops/unary_out.cpp:46-51,
+ * raw_unary_value<Silu>): one thread, element by element, fp32 arithmetic,
+ * rounded to bf16.  `rows` rows of `d` values at row pitch `pitch`
+ * (elements) in, dense [rows, d] out. */
+void oracle_silu_raw_bf16(const uint16_t* x, int64_t rows, int64_t d, int64_t pitch, uint16_t* out,
+                          int exp_mode) {
+  for (int64_t r = 0; r < rows; ++r)
+    for (int64_t j = 0; j < d; ++j)
+      out[r * d + j] = f32_to_bf16(silu_f(bf16_to_f32(x[r * pitch + j]), exp_mode));
+}

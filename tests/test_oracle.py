@@ -156,3 +156,32 @@ def test_oracle_rejects_bad_arguments():
         oracle.grouped_topk(g, 2, True, 3, 1, "softmax")  # 10 % 3 != 0
     with pytest.raises(ValueError):
         oracle.grouped_topk(g, 9, True, 5, 1, "softmax")  # k > topk_group * group size
+
+
+@pytest.mark.parametrize("cfg", [c for c in C.ROUTER_GOLDEN if c.dtype == "float32"], ids=lambda c: c.name)
+def test_router_op_chain_restatement_matches_reference_fixtures(cfg):
+    """oracle/aten_chain.py (the reference's router op by op, timed as the
+    CPU baseline) gives the reference fixtures' ids and weights."""
+    from oracle import aten_chain
+
+    fx = np.load(os.path.join(GOLDEN, f"router_{cfg.name}.npz"))
+    gating, bias = C.router_inputs(cfg)
+    w, ids = aten_chain.grouped_topk_chain(gating, cfg.K, cfg.renorm, cfg.G, cfg.TG, cfg.scoring, cfg.scale,
+                                           bias)
+    ws, idss = _by_id(w.numpy(), ids.numpy())
+    ok = ~fx["ambiguous"]
+    np.testing.assert_array_equal(idss[ok], fx["ids_sorted"][ok].astype(np.int32))
+    np.testing.assert_allclose(ws[ok], fx["weights_by_id"][ok], rtol=1e-6, atol=0)
+
+
+def test_silu_and_rms_op_chains_match_the_oracle():
+    from oracle import aten_chain
+
+    x = C.silu_inputs(33, 1000)
+    got = aten_chain.silu_and_mul_chain(x).view(torch.int16).numpy().view(np.uint16)
+    assert np.array_equal(got, oracle.silu_and_mul_bf16(x.view(torch.int16).numpy().view(np.uint16)))
+    x, w = C.rms_inputs(9, 4096)
+    got = aten_chain.rms_norm_chain(x, w, C.RMS_EPS).view(torch.int16).numpy().view(np.uint16)
+    want = oracle.rms_norm_bf16(x.view(torch.int16).numpy().view(np.uint16), w.view(torch.int16).numpy().view(np.uint16),
+                                C.RMS_EPS)
+    assert np.array_equal(got, want)

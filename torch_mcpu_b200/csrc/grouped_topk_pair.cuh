@@ -111,13 +111,16 @@ __device__ __forceinline__ void top2_add4(float& m1, float& m2, float k0, float 
   m1 = fmaxf(m1, t1);
 }
 
+// Inserts v into the descending list (the last entry drops out): slot i
+// becomes max(L[i], min(L[i - 1], v)), every slot from the old list, so the
+// update is two operations deep.
 __device__ __forceinline__ void list_insert(uint32_t (&lst)[kPairList], uint32_t v) {
+  uint32_t n[kPairList];
+  n[0] = max(lst[0], v);
 #pragma unroll
-  for (int i = 0; i < kPairList; ++i) {
-    const uint32_t hi = max(lst[i], v);
-    v = min(lst[i], v);
-    lst[i] = hi;
-  }
+  for (int i = 1; i < kPairList; ++i) n[i] = max(lst[i], min(lst[i - 1], v));
+#pragma unroll
+  for (int i = 0; i < kPairList; ++i) lst[i] = n[i];
 }
 
 // 64-bit max across the warp (butterfly).
@@ -256,16 +259,18 @@ __global__ void __launch_bounds__(NW * 32, 1) grouped_topk_pair_kernel(
     const long long token = wt * kPairTokens + t;
     const bool valid = token < p.T;
 
-    // ---- keys of this lane's four groups, written over the logits
+    // ---- keys of this lane's four groups, written over the logits (chunk
+    // by chunk across the four groups: four independent top-2 chains)
     float gsh[4], m2h[4];
     {
       char* hb = tb + h * 4 * kPairBox + rowoff;
       const float* bh = sbias + h * 4 * kPairGS;
+      float m1[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      float m2v[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int gg = 0; gg < 4; ++gg) {
-        float m1 = -INFINITY, m2 = -INFINITY;
+      for (int c = 0; c < kPairGS / 4; ++c) {
 #pragma unroll
-        for (int c = 0; c < kPairGS / 4; ++c) {
+        for (int gg = 0; gg < 4; ++gg) {
           float4* px = reinterpret_cast<float4*>(hb + gg * kPairBox + ((c << 4) ^ x7));
           const float4 x4 = *px;
           const float4 b4 = *reinterpret_cast<const float4*>(bh + gg * kPairGS + c * 4);
@@ -273,10 +278,13 @@ __global__ void __launch_bounds__(NW * 32, 1) grouped_topk_pair_kernel(
           fast_key2(x4.x, x4.y, b4.x, b4.y, k4.x, k4.y);
           fast_key2(x4.z, x4.w, b4.z, b4.w, k4.z, k4.w);
           *px = k4;
-          top2_add4(m1, m2, k4.x, k4.y, k4.z, k4.w);
+          top2_add4(m1[gg], m2v[gg], k4.x, k4.y, k4.z, k4.w);
         }
-        m2h[gg] = m2;
-        gsh[gg] = __fadd_rn(m1, m2);
+      }
+#pragma unroll
+      for (int gg = 0; gg < 4; ++gg) {
+        m2h[gg] = m2v[gg];
+        gsh[gg] = __fadd_rn(m1[gg], m2v[gg]);
       }
     }
     // ---- the two lanes swap their group scores; group pick (ties to the
@@ -349,41 +357,59 @@ __global__ void __launch_bounds__(NW * 32, 1) grouped_topk_pair_kernel(
 #pragma unroll
     for (int i = 0; i < kPairList; ++i) lst[i] = 0u;
     {
-      uint32_t r0 = slow ? 0u : cm[0], r1 = slow ? 0u : cm[1];
-      while (r0 | r1) {
-        int g;
-        uint32_t m;
-        if (r0) {
-          m = r0;
-          g = cg[0];
-          r0 &= r0 - 1;
-        } else {
-          m = r1;
-          g = cg[1];
-          r1 &= r1 - 1;
-        }
-        const int j = __ffs(m) - 1;
+      unsigned long long mm = slow ? 0ull : (cm[0] | (static_cast<unsigned long long>(cm[1]) << 32));
+      while (mm) {
+        const int i = __ffsll(mm) - 1;
+        mm &= mm - 1;
+        const int g = i < 32 ? cg[0] : cg[1];
+        const int j = i & 31;
         const float key = *reinterpret_cast<const float*>(tb + pair_elem_off(rowoff, x7, g, j));
         list_insert(lst, (__float_as_uint(__fsub_rn(key, thr)) & ~255u) |
                              static_cast<uint32_t>(255 - (g * kPairGS + j)));
       }
     }
+    // merge with the partner's list: the picks (K of them) in pk[0 .. K-1]
+    // (any order), and the K-th / (K+1)-th best packed keys lk, ln
+    uint32_t pk[kPairKMax];
+    uint32_t lk, ln;
     {
       uint32_t o[kPairList];
 #pragma unroll
       for (int i = 0; i < kPairList; ++i) o[i] = __shfl_xor_sync(0xFFFFFFFFu, lst[i], 16);
+      if (K == kPairKMax) {
+        // both lists descending: c[i] = max(A[i], B[8 - i]) is the best nine
+        // of the union (in bitonic order); the ninth is its minimum, the
+        // eighth the minimum of the rest
+        uint32_t c[kPairList];
 #pragma unroll
-      for (int i = 0; i < kPairList; ++i) list_insert(lst, o[i]);
+        for (int i = 0; i < kPairList; ++i) c[i] = max(lst[i], o[kPairList - 1 - i]);
+        uint32_t mn = c[0];
+#pragma unroll
+        for (int i = 1; i < kPairList; ++i) mn = min(mn, c[i]);
+        uint32_t sm = 0xFFFFFFFFu;
+#pragma unroll
+        for (int i = 0; i < kPairList; ++i) sm = min(sm, c[i] == mn ? 0xFFFFFFFFu : c[i]);
+        ln = mn;
+        lk = sm;
+#pragma unroll
+        for (int i = 0; i < kPairKMax; ++i) pk[i] = c[i] == mn ? c[kPairList - 1] : c[i];
+      } else {
+#pragma unroll
+        for (int i = 0; i < kPairList; ++i) list_insert(lst, o[i]);
+        lk = lst[0];
+        ln = lst[0];
+#pragma unroll
+        for (int i = 0; i < kPairList; ++i) {
+          if (i == K - 1) lk = lst[i];
+          if (i == K) ln = lst[i];
+        }
+#pragma unroll
+        for (int i = 0; i < kPairKMax; ++i) pk[i] = lst[i];
+      }
     }
     // the K-th / (K+1)-th boundary, from the truncation buckets' edges in
     // key - thr space: every pick is >= lo, every other candidate <= hi
     if (!slow && C > K) {
-      uint32_t lk = lst[0], ln = lst[0];
-#pragma unroll
-      for (int i = 0; i < kPairList; ++i) {
-        if (i == K - 1) lk = lst[i];
-        if (i == K) ln = lst[i];
-      }
       bool cert = false;
       if ((lk >> 8) > (ln >> 8)) {
         const float lo = __uint_as_float(lk & ~255u), hi = __uint_as_float(ln | 255u);
@@ -397,7 +423,7 @@ __global__ void __launch_bounds__(NW * 32, 1) grouped_topk_pair_kernel(
     float pkv[4];
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
-      const uint32_t e8 = h ? lst[4 + u] : lst[u];
+      const uint32_t e8 = h ? pk[4 + u] : pk[u];
       pid[u] = 255 - static_cast<int>(e8 & 255u);
       pkv[u] = *reinterpret_cast<const float*>(tb + pair_elem_off(rowoff, x7, pid[u] >> 5, pid[u] & 31));
     }
