@@ -147,12 +147,13 @@ KERNEL_CASES = [C.deepseek_v3(t) for t in (1, 16, 33, 256, 1000, 4096, 65536)] +
 ]
 
 
-@pytest.mark.parametrize("kernel", ["pair", "quad"])
+@pytest.mark.parametrize("kernel", ["lanes4", "pair", "quad"])
 @pytest.mark.parametrize("cfg", KERNEL_CASES, ids=lambda c: c.name)
 def test_router_pair_and_quad_kernels_at_every_size(cfg, kernel, monkeypatch):
     """The DeepSeek-V3 shape (256 experts, 8 groups, fp32, sigmoid + bias) is
-    served by the pair kernel (two lanes per token) from 8192 tokens and by
-    the quad kernel (four lanes per token) below; each is forced here over
+    served by the four-lane kernel (topk_group 4, topk 8), the pair kernel
+    (two lanes per token, other topk_group / topk, from 8192 tokens) or the
+    first quad kernel (below 8192 tokens); each is forced here over
     ragged, tiny and full-size batches and other topk_group / topk choices."""
     monkeypatch.setenv("MCPU_ROUTER_KERNEL", kernel)
     gating, bias = C.router_inputs(cfg)
@@ -161,7 +162,7 @@ def test_router_pair_and_quad_kernels_at_every_size(cfg, kernel, monkeypatch):
     _assert_parity(cfg, w, ids, ow, oids, oties, 1e-6)
 
 
-@pytest.mark.parametrize("kernel", ["pair", "quad"])
+@pytest.mark.parametrize("kernel", ["lanes4", "pair", "quad"])
 def test_router_many_equal_keys_take_the_exact_paths(kernel, monkeypatch):
     """Rows whose keys tie in many places: all keys equal (every group and
     expert margin is zero), and rows where a whole group ties, so the

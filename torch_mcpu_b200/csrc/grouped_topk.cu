@@ -318,6 +318,7 @@ __global__ void __launch_bounds__(kThreads) grouped_topk_kernel(const Params p) 
 #include "grouped_topk_g8.cuh"
 #include "grouped_topk_quad.cuh"
 #include "grouped_topk_pair.cuh"
+#include "grouped_topk_lanes4.cuh"
 
 
 namespace mcpu {
@@ -435,10 +436,49 @@ static cudaError_t launch_pair(const Params& p, cudaStream_t st, EncodeTiledFn e
   return cudaGetLastError();
 }
 
+template <int NW>
+static cudaError_t launch_lanes4(const Params& p, cudaStream_t st, EncodeTiledFn enc) {
+  auto kern = grouped_topk_lanes4_kernel<NW>;
+  constexpr L4Layout L = l4_layout(NW);
+  {
+    cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), L.total);
+    if (e != cudaSuccess) return e;
+  }
+  CUtensorMap tm;
+  cuuint64_t gdim[2] = {static_cast<cuuint64_t>(kPairE), static_cast<cuuint64_t>(p.T)};
+  cuuint64_t gstride[1] = {static_cast<cuuint64_t>(kPairE) * 4};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(kPairGS), static_cast<cuuint32_t>(kL4Tokens)};
+  cuuint32_t estr[2] = {1, 1};
+  if (enc(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(p.gating), gdim, gstride, box, estr,
+          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return cudaErrorInvalidValue;
+  const long long wtiles = (p.T + kL4Tokens - 1) / kL4Tokens;
+  const long long ctas_needed = (wtiles + NW - 1) / NW;
+  const long long cap = device_sms();  // one CTA per SM
+  const int grid = static_cast<int>(ctas_needed < cap ? ctas_needed : cap);
+  const int vec_out = reinterpret_cast<uintptr_t>(p.w_out) % 8 == 0 && reinterpret_cast<uintptr_t>(p.id_out) % 8 == 0;
+  kern<<<grid, NW * 32, L.total, st>>>(tm, p, wtiles, vec_out);
+  return cudaGetLastError();
+}
+
+// Warps per SM of the four-lane kernel (8 KB slot each).
+constexpr int kL4Warps = 28;
+
 // Tokens from which the pair kernel (two lanes per token) serves the
 // DeepSeek-V3 shape; below, the quad kernel (four lanes per token) spreads a
 // small batch over more warps.  MCPU_ROUTER_KERNEL=pair|quad forces a choice.
 constexpr long long kPairMinTokens = 8192;
+
+// The four-lane kernel serves DeepSeek-V3's exact shape (topk_group 4,
+// topk 8); MCPU_ROUTER_KERNEL=lanes4|pair|quad forces a choice.
+static bool use_lanes4_kernel(const Params& p) {
+  if (!(p.E == kPairE && p.G == kPairG && p.TG == 4 && p.K == kPairKMax)) return false;
+  if (p.T >= (1LL << 31) - kL4Tokens) return false;
+  const char* force = getenv("MCPU_ROUTER_KERNEL");
+  if (force) return strcmp(force, "lanes4") == 0;
+  return true;
+}
 
 static bool use_pair_kernel(const Params& p) {
   if (!(p.E == kPairE && p.G == kPairG && p.TG <= kPairTGMax && p.K <= kPairKMax && 2 * p.TG >= p.K)) return false;
@@ -484,6 +524,11 @@ static orError_t launch_hot(Params p, int dtype, bool fast, cudaStream_t st, boo
   static EncodeTiledFn enc = reinterpret_cast<EncodeTiledFn>(driver_entry("cuTensorMapEncodeTiled"));
   if (!enc) return orSuccess;
   if (!(p.G == 8 || (esz == 4 && (p.G == 4 || p.G == 16 || p.G == 32)))) return orSuccess;
+  // fp32 sigmoid + bias, 256 experts in 8 groups, topk_group 4, topk 8
+  if (fast && use_lanes4_kernel(p)) {
+    *handled = true;
+    return from_cuda(launch_lanes4<kL4Warps>(p, st, enc), "grouped_topk launch");
+  }
   // fp32 sigmoid + bias, 256 experts in 8 groups, large batches: the pair kernel
   if (fast && use_pair_kernel(p)) {
     *handled = true;

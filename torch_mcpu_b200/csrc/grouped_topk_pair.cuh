@@ -139,8 +139,9 @@ __device__ __forceinline__ unsigned long long warp_max_u64(unsigned long long v)
 // with ties to the lower group; then topk rounds of a warp arg-max over the
 // picked groups' packed (key, inverted index) pairs.  Writes the token's
 // outputs.
-__device__ __noinline__ void pair_warp_exact_pick(const float* gx, const float* sbias, const Params& p,
-                                                  long long token, int lane) {
+__device__ __noinline__ void pair_warp_exact_pick(const float* gx, const float* sbias, int TG, int K, int renorm,
+                                                  float scale, float* w_out, int32_t* id_out, long long token,
+                                                  int lane) {
   const float4 xa = __ldg(reinterpret_cast<const float4*>(gx) + 2 * lane);
   const float4 xb = __ldg(reinterpret_cast<const float4*>(gx) + 2 * lane + 1);
   const float x[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
@@ -168,13 +169,13 @@ __device__ __noinline__ void pair_warp_exact_pick(const float* gx, const float* 
     const float o = __shfl_sync(0xFFFFFFFFu, gsc, 4 * j);
     r += (o > gsc) || (o == gsc && j < g);
   }
-  const bool sel = r < p.TG;
+  const bool sel = r < TG;
   unsigned long long pk[8];
 #pragma unroll
   for (int u = 0; u < 8; ++u) pk[u] = sel ? pack_key(key[u], 8 * lane + u) : 0ull;
   float myw = 0.0f;
   int myid = 0;
-  for (int k = 0; k < p.K; ++k) {
+  for (int k = 0; k < K; ++k) {
     unsigned long long best = 0ull;
     float bsg = 0.0f;
 #pragma unroll
@@ -196,13 +197,13 @@ __device__ __noinline__ void pair_warp_exact_pick(const float* gx, const float* 
     }
   }
   float sum = 0.0f;
-  for (int k = 0; k < p.K; ++k) sum = __fadd_rn(sum, __shfl_sync(0xFFFFFFFFu, myw, k));
-  if (lane < p.K) {
+  for (int k = 0; k < K; ++k) sum = __fadd_rn(sum, __shfl_sync(0xFFFFFFFFu, myw, k));
+  if (lane < K) {
     float w = myw;
-    if (p.renorm) w = __fdiv_rn(w, sum);
-    if (p.scale != 1.0f) w = __fmul_rn(w, p.scale);
-    p.w_out[token * p.K + lane] = w;
-    p.id_out[token * p.K + lane] = myid;
+    if (renorm) w = __fdiv_rn(w, sum);
+    if (scale != 1.0f) w = __fmul_rn(w, scale);
+    w_out[token * K + lane] = w;
+    id_out[token * K + lane] = myid;
   }
 }
 
@@ -380,9 +381,12 @@ __global__ void __launch_bounds__(NW * 32, 1) grouped_topk_pair_kernel(
         // both lists descending: c[i] = max(A[i], B[8 - i]) is the best nine
         // of the union (in bitonic order); the ninth is its minimum, the
         // eighth the minimum of the rest
+        // (both lanes orient it the same way, lane t's list first, so that
+        // the two halves take their picks from the same order)
         uint32_t c[kPairList];
 #pragma unroll
-        for (int i = 0; i < kPairList; ++i) c[i] = max(lst[i], o[kPairList - 1 - i]);
+        for (int i = 0; i < kPairList; ++i)
+          c[i] = max(h ? o[i] : lst[i], h ? lst[kPairList - 1 - i] : o[kPairList - 1 - i]);
         uint32_t mn = c[0];
 #pragma unroll
         for (int i = 1; i < kPairList; ++i) mn = min(mn, c[i]);
@@ -485,7 +489,7 @@ __global__ void __launch_bounds__(NW * 32, 1) grouped_topk_pair_kernel(
       const int src = __ffs(pending) - 1;
       pending &= pending - 1;
       const long long tok = wt * kPairTokens + src;
-      pair_warp_exact_pick(gating + tok * kPairE, sbias, p, tok, lane);
+      pair_warp_exact_pick(gating + tok * kPairE, sbias, TG, K, p.renorm, p.scale, p.w_out, p.id_out, tok, lane);
       if (lane == 0) atomicAdd(&g_exact_rows, 1ull);
     }
   }
