@@ -1,7 +1,12 @@
 """grouped_topk on the B200 against the oracle and the reference's fixtures.
 
 Parity bar: topk_ids bit-exact as per-row sets (the reference's own order is
-an ATen artefact), topk_weights matched by id within 1e-5 relative (fp32).
+an ATen artefact), topk_weights matched by id within 1e-6 relative (fp32
+logits) or within one bf16 ulp, 2^-8 relative (bf16 logits: the reference
+rounds the scores, the renormalisation sum and the weights to bf16, and the
+GPU rounds at the same points; only the order of the eight-term sum, which
+the reference takes in its own topk output order, can move a weight by one
+ulp).  The oracle itself matches the reference's bf16 fixtures bit for bit.
 Every call goes through the C-ABI entry point mcpu_grouped_topk.
 """
 
@@ -20,6 +25,7 @@ pytestmark = pytest.mark.gpu
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
 MANIFEST = json.load(open(os.path.join(GOLDEN, "manifest.json")))
 DEV = "cuda:0"
+BF16_ULP = 2.0 ** -8
 
 
 def _mcpu():
@@ -64,13 +70,13 @@ def test_router_matches_oracle_and_reference(cfg):
     gating, bias = C.router_inputs(cfg)
     w, ids = _gpu(cfg, gating, bias)
     ow, oids, oties, _ = _oracle(cfg, gating, bias)
-    rtol = 1e-6 if cfg.dtype == "float32" else 8e-3
+    rtol = 1e-6 if cfg.dtype == "float32" else BF16_ULP
     _assert_parity(cfg, w, ids, ow, oids, oties, rtol)
     fx = np.load(os.path.join(GOLDEN, f"router_{cfg.name}.npz"))
     ok = ~fx["ambiguous"]
     ws, idss = _by_id(w, ids)
     np.testing.assert_array_equal(idss[ok], fx["ids_sorted"][ok].astype(np.int32))
-    np.testing.assert_allclose(ws[ok], fx["weights_by_id"][ok], rtol=1e-5 if cfg.dtype == "float32" else 8e-3)
+    np.testing.assert_allclose(ws[ok], fx["weights_by_id"][ok], rtol=1e-5 if cfg.dtype == "float32" else BF16_ULP)
 
 
 @pytest.mark.parametrize("cfg", C.ROUTER_LARGE, ids=lambda c: c.name)
@@ -103,7 +109,7 @@ def test_reference_regression_case_bf16_softmax():
     ws, idss = _by_id(w.cpu().numpy(), ids.cpu().numpy())
     ok = ~fx["ambiguous"]
     np.testing.assert_array_equal(idss[ok], fx["ids_sorted"][ok].astype(np.int32))
-    np.testing.assert_allclose(ws[ok], fx["weights_by_id"][ok], rtol=8e-3)
+    np.testing.assert_allclose(ws[ok], fx["weights_by_id"][ok], rtol=BF16_ULP)
 
 
 EDGE = [
@@ -135,7 +141,7 @@ def test_router_edge_configurations(cfg):
         np.testing.assert_array_equal(idss[keep], oidss[keep])
         np.testing.assert_allclose(ws[keep], ows[keep], rtol=1e-5)
         return
-    rtol = 1e-6 if cfg.dtype == "float32" else 8e-3
+    rtol = 1e-6 if cfg.dtype == "float32" else BF16_ULP
     _assert_parity(cfg, w, ids, ow, oids, oties, rtol)
 
 
