@@ -517,13 +517,40 @@ def bandwidth_leg(dev, reps=20):
     return out
 
 
-def moe_leg(dev, ids, stream, reps=8, per_graph=32):
-    """MoE dispatch after the router: moe_align_block_size on the router's
-    own topk_ids [65536, 8] (256 experts, block 64), replayed from a CUDA
-    graph; time per call and GB/s of its algorithmic bytes (ids read once,
-    sorted ids and block experts written once)."""
-    import ctypes
+def _graph_us(stream, launch, reps, per_graph):
+    """us per launch of `launch(i)` replayed from a CUDA graph of per_graph
+    launches (after 3 eager warm-ups and one untimed replay)."""
+    import torch
 
+    with torch.cuda.stream(stream):
+        for i in range(3):
+            launch(i)
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(per_graph):
+            launch(i)
+    _upload(graph, stream)
+    with torch.cuda.stream(stream):
+        graph.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(stream)
+    e1.synchronize()
+    del graph
+    return e0.elapsed_time(e1) * 1e3 / (reps * per_graph)
+
+
+def moe_leg(dev, ids, stream, bufs, bias, reps=8, per_graph=32):
+    """MoE dispatch after the router.  (1) moe_align_block_size alone on the
+    router's own topk_ids [65536, 8] (256 experts, block 64): time per call
+    and GB/s of its algorithmic bytes (ids read once, sorted ids and block
+    experts written once).  (2) Router + dispatch per batch over the
+    router's rotating inputs: the router alone, the router then
+    moe_align_block_size (three launches), and mcpu_grouped_topk_moe_align
+    (one launch), whose outputs are first checked equal to the two calls'."""
     import torch
 
     from torch_mcpu_b200 import _lib
@@ -540,34 +567,63 @@ def moe_leg(dev, ids, stream, reps=8, per_graph=32):
     _lib.check(lib.mcpu_moe_align_workspace_bytes(numel, E_, ctypes.byref(wsb)), "moe workspace")
     work = torch.empty(wsb.value, dtype=torch.uint8, device=dev)
 
-    def call():
-        _lib.check(lib.mcpu_moe_align_block_size(ids.data_ptr(), numel, E_, bs, srt.data_ptr(), cap, eid.data_ptr(),
+    def align(i, src=ids):
+        _lib.check(lib.mcpu_moe_align_block_size(src.data_ptr(), numel, E_, bs, srt.data_ptr(), cap, eid.data_ptr(),
                                                  nblk, npad.data_ptr(), work.data_ptr(), wsb.value,
                                                  stream.cuda_stream), "moe_align_block_size")
 
-    with torch.cuda.stream(stream):
-        for _ in range(3):
-            call()
-    stream.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream):
-        for _ in range(per_graph):
-            call()
-    with torch.cuda.stream(stream):
-        graph.replay()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(reps):
-            graph.replay()
-        e1.record(stream)
-    e1.synchronize()
-    us = e0.elapsed_time(e1) * 1e3 / (reps * per_graph)
-    del graph
+    us = _graph_us(stream, align, reps, per_graph)
     nbytes = numel * 4 + cap * 4 + nblk * 4 + 4
     gbs = nbytes / (us * 1e-6) / 1e9
-    return {"shape": f"topk_ids int32 [{numel // 8}, 8] from the router, {E_} experts, block {bs}",
-            "us_per_call": round(us, 2), "launches_per_call": 2, "algorithmic_bytes": nbytes,
-            "achieved_gbs": round(gbs, 1), "peak_gbs": peak, "frac": round(gbs / peak, 4), "peak_kind": peak_kind}
+    out = {"shape": f"topk_ids int32 [{numel // 8}, 8] from the router, {E_} experts, block {bs}",
+           "us_per_call": round(us, 2), "launches_per_call": 2, "algorithmic_bytes": nbytes,
+           "achieved_gbs": round(gbs, 1), "peak_gbs": peak, "frac": round(gbs / peak, 4), "peak_kind": peak_kind}
+
+    # router + dispatch over the rotating inputs
+    w2 = torch.empty(T, K, dtype=torch.float32, device=dev)
+    ids2 = torch.empty(T, K, dtype=torch.int32, device=dev)
+    fwsb = ctypes.c_uint64()
+    _lib.check(lib.mcpu_grouped_topk_moe_align_workspace_bytes(T, E_, K, ctypes.byref(fwsb)), "fused workspace")
+    fwork = torch.zeros(fwsb.value, dtype=torch.uint8, device=dev)
+    fsrt = torch.empty(cap, dtype=torch.int32, device=dev)
+    feid = torch.empty(nblk, dtype=torch.int32, device=dev)
+    fnpad = torch.empty(1, dtype=torch.int32, device=dev)
+
+    def route(i):
+        _lib.check(lib.mcpu_grouped_topk(bufs[i % N_BUFFERS].data_ptr(), 0, T, E_, G, TG, K, 1, 2.5,
+                                         bias.data_ptr(), 1, w2.data_ptr(), ids2.data_ptr(), stream.cuda_stream),
+                   "grouped_topk")
+
+    def route_then_align(i):
+        route(i)
+        align(i, ids2)
+
+    def fused(i):
+        _lib.check(lib.mcpu_grouped_topk_moe_align(
+            bufs[i % N_BUFFERS].data_ptr(), 0, T, E_, G, TG, K, 1, 2.5, bias.data_ptr(), 1, w2.data_ptr(),
+            ids2.data_ptr(), bs, fsrt.data_ptr(), cap, feid.data_ptr(), nblk, fnpad.data_ptr(), fwork.data_ptr(),
+            fwsb.value, stream.cuda_stream), "grouped_topk_moe_align")
+
+    with torch.cuda.stream(stream):
+        route_then_align(1)
+        fused(1)
+    stream.synchronize()
+    if not (torch.equal(fsrt, srt) and torch.equal(feid, eid) and torch.equal(fnpad, npad)):
+        raise SystemExit("bench: fused router + dispatch differs from the router then moe_align_block_size")
+    us_router = _graph_us(stream, route, reps, per_graph)
+    us_two = _graph_us(stream, route_then_align, reps, per_graph)
+    us_fused = _graph_us(stream, fused, reps, per_graph)
+    out["router_then_dispatch"] = {
+        "config": f"T={T} E={E_} topk={K} block {bs}, {N_BUFFERS} rotating {T * E_ * 4 / 1e6:.1f} MB inputs, "
+                  f"graph replay of {per_graph} calls",
+        "router_us": round(us_router, 2),
+        "router_then_moe_align_us": round(us_two, 2),
+        "fused_us": round(us_fused, 2),
+        "fused_minus_router_us": round(us_fused - us_router, 2),
+        "launches": {"router": 1, "router_then_moe_align": 3, "fused": 1},
+        "fused_mtok_s": round(T / (us_fused * 1e-6) / 1e6, 1),
+    }
+    return out
 
 
 def sampler_leg(dev, reps=20):
@@ -898,7 +954,7 @@ def run_ours(a):
 
     sweep = leg("sweep", lambda: router_sweep_leg(lib, dev, stream)) if "sweep" in a.legs else None
     bw = leg("bw", lambda: bandwidth_leg(dev)) if "bw" in a.legs else None
-    moe = leg("moe", lambda: moe_leg(dev, ids, stream)) if "moe" in a.legs else None
+    moe = leg("moe", lambda: moe_leg(dev, ids, stream, bufs, bias)) if "moe" in a.legs else None
     sampler = leg("sampler", lambda: sampler_leg(dev)) if "sampler" in a.legs else None
     mlp = None
     if "mlp" in a.legs:

@@ -82,6 +82,42 @@ OPENREG_EXPORT orError_t mcpu_grouped_topk_exact_rows(
     unsigned long long* count, int reset);
 
 /*
+ * grouped_topk_moe_align: the router followed by the expert dispatch, i.e.
+ * mcpu_grouped_topk (arguments and outputs as above) and then
+ * mcpu_moe_align_block_size on its topk_ids (numel = num_tokens * topk,
+ * num_experts experts; block_size and the last five outputs as there) --
+ * vLLM's fused-MoE sequence grouped_topk -> moe_align_block_size
+ * (vllm/model_executor/layers/fused_moe/moe_align_block_size.py:19-73).
+ * Results are bit-identical to the two calls.
+ *
+ * For DeepSeek-V3's router (fp32 logits, 256 experts in 8 groups,
+ * topk_group 4, topk 8, sigmoid + bias) it is ONE cooperative launch: each
+ * CTA routes a contiguous token range, counts its ids per expert, sorts
+ * them by expert in shared memory, and after one grid-wide barrier (bounded:
+ * a wait that runs out after 2 s sets mcpu_device_error) copies them to
+ * their places.  Other configurations, or more than 65535 ids per SM, run
+ * the router and the dispatch's two launches.
+ *
+ * workspace: device memory of
+ * mcpu_grouped_topk_moe_align_workspace_bytes(num_tokens, num_experts, topk)
+ * bytes (sized for the current device), 16-byte aligned and zero-filled
+ * before its first call (e.g. one cudaMemset when it is allocated).  Each
+ * call leaves it ready for the next, so one workspace serves any number of
+ * calls ordered on one stream.  After a device error, zero-fill it again.
+ * No counterpart in the reference (it runs the router's aten chain and has
+ * no dispatch op).
+ */
+OPENREG_EXPORT orError_t mcpu_grouped_topk_moe_align(
+    const void* gating, int gating_dtype, int64_t num_tokens, int num_experts, int num_expert_group,
+    int topk_group, int topk, int renormalize, float routed_scaling_factor, const float* bias,
+    int scoring_func, float* topk_weights, int32_t* topk_ids, int block_size, int32_t* sorted_token_ids,
+    int64_t sorted_capacity, int32_t* expert_ids, int64_t expert_ids_capacity, int32_t* num_tokens_post_pad,
+    void* workspace, uint64_t workspace_bytes, orStream_t stream);
+
+OPENREG_EXPORT orError_t mcpu_grouped_topk_moe_align_workspace_bytes(int64_t num_tokens, int num_experts,
+                                                                     int topk, uint64_t* bytes);
+
+/*
  * silu_and_mul: out[t, j] = silu(x[t, j]) * x[t, d + j] for x [T, 2d],
  * out [T, d], both contiguous bf16 on the device.
  *

@@ -65,6 +65,10 @@ SIGNATURES = {
     "mcpu_grouped_topk": (c_int, [c_void_p, c_int, c_int64, c_int, c_int, c_int, c_int, c_int,
                                   c_float, c_void_p, c_int, c_void_p, c_void_p, c_void_p]),
     "mcpu_grouped_topk_exact_rows": (c_int, [ctypes.POINTER(ctypes.c_ulonglong), c_int]),
+    "mcpu_grouped_topk_moe_align": (c_int, [c_void_p, c_int, c_int64, c_int, c_int, c_int, c_int, c_int, c_float,
+                                            c_void_p, c_int, c_void_p, c_void_p, c_int, c_void_p, c_int64, c_void_p,
+                                            c_int64, c_void_p, c_void_p, ctypes.c_uint64, c_void_p]),
+    "mcpu_grouped_topk_moe_align_workspace_bytes": (c_int, [c_int64, c_int, c_int, ctypes.POINTER(ctypes.c_uint64)]),
     "mcpu_silu_and_mul": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int, c_void_p]),
     "mcpu_rms_norm": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_float, c_int, c_void_p]),
     "mcpu_mm": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int, c_void_p]),

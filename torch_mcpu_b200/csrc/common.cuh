@@ -36,6 +36,17 @@ orError_t read_error(int* flag, bool reset);
 }
 orError_t aten_read_error(int* flag, bool reset);
 orError_t moe_read_error(int* flag, bool reset);
+
+// moe_align_block_size's argument check and its two launches (moe_align.cu),
+// also behind the router + dispatch entry point when that is not one launch.
+namespace moe {
+orError_t check_args(const int32_t* topk_ids, long long numel, int E, int bs, const int32_t* sorted,
+                     long long sorted_cap, const int32_t* expert_ids, long long eid_cap, const int32_t* post_pad,
+                     int* nchunks_out);
+orError_t launch(const int32_t* topk_ids, long long numel, int E, int bs, int32_t* sorted, long long sorted_cap,
+                 int32_t* expert_ids, long long eid_cap, int32_t* post_pad, int32_t* ws, int nchunks,
+                 cudaStream_t st);
+}  // namespace moe
 orError_t sampler_read_error(int* flag, bool reset);
 
 inline cudaStream_t as_cuda(orStream_t s) {

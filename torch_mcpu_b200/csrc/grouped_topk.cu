@@ -436,9 +436,13 @@ static cudaError_t launch_pair(const Params& p, cudaStream_t st, EncodeTiledFn e
   return cudaGetLastError();
 }
 
-template <int NW>
-static cudaError_t launch_lanes4(const Params& p, cudaStream_t st, EncodeTiledFn enc) {
-  auto kern = grouped_topk_lanes4_kernel<NW>;
+// The four-lane kernel; with kDispatch the variant that also writes the
+// expert dispatch (*dispatch), as one cooperative launch of at most
+// grid_req CTAs (<= the SM count; 0: the SM count).
+template <int NW, bool kDispatch>
+static cudaError_t launch_lanes4(const Params& p, cudaStream_t st, EncodeTiledFn enc,
+                                 const Dispatch* dispatch = nullptr, int grid_req = 0) {
+  auto kern = grouped_topk_lanes4_kernel<NW, kDispatch>;
   constexpr L4Layout L = l4_layout(NW);
   {
     cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(kern), L.total);
@@ -455,12 +459,30 @@ static cudaError_t launch_lanes4(const Params& p, cudaStream_t st, EncodeTiledFn
     return cudaErrorInvalidValue;
   const long long wtiles = (p.T + kL4Tokens - 1) / kL4Tokens;
   const long long ctas_needed = (wtiles + NW - 1) / NW;
-  const long long cap = device_sms();  // one CTA per SM
+  const long long cap = grid_req > 0 ? grid_req : device_sms();  // one CTA per SM
   const int grid = static_cast<int>(ctas_needed < cap ? ctas_needed : cap);
   const int vec_out = reinterpret_cast<uintptr_t>(p.w_out) % 8 == 0 && reinterpret_cast<uintptr_t>(p.id_out) % 8 == 0;
-  kern<<<grid, NW * 32, L.total, st>>>(tm, p, wtiles, vec_out);
-  return cudaGetLastError();
+  if constexpr (kDispatch) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(NW * 32);
+    cfg.dynamicSmemBytes = L.total;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;  // the dispatch's grid barrier needs every CTA resident
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, tm, p, wtiles, vec_out, *dispatch);
+  } else {
+    kern<<<grid, NW * 32, L.total, st>>>(tm, p, wtiles, vec_out, Dispatch{});
+    return cudaGetLastError();
+  }
 }
+
+// Largest number of tiles one CTA of the fused dispatch may route: its
+// expert counts are kept as 16-bit values (at most 8 ids per token).
+constexpr long long kL4DispatchMaxTiles = 65535 / (kL4Tokens * kPairKMax);
 
 // Warps per SM of the four-lane kernel (8 KB slot each).
 constexpr int kL4Warps = 28;
@@ -527,7 +549,7 @@ static orError_t launch_hot(Params p, int dtype, bool fast, cudaStream_t st, boo
   // fp32 sigmoid + bias, 256 experts in 8 groups, topk_group 4, topk 8
   if (fast && use_lanes4_kernel(p)) {
     *handled = true;
-    return from_cuda(launch_lanes4<kL4Warps>(p, st, enc), "grouped_topk launch");
+    return from_cuda(launch_lanes4<kL4Warps, false>(p, st, enc), "grouped_topk launch");
   }
   // fp32 sigmoid + bias, 256 experts in 8 groups, large batches: the pair kernel
   if (fast && use_pair_kernel(p)) {
@@ -636,11 +658,14 @@ static cudaError_t launch2(const Params& p, bool vec, cudaStream_t st) {
 
 using namespace mcpu;
 
-extern "C" orError_t mcpu_grouped_topk(const void* gating, int gating_dtype, int64_t num_tokens,
-                                       int num_experts, int num_expert_group, int topk_group,
-                                       int topk, int renormalize, float routed_scaling_factor,
-                                       const float* bias, int scoring_func, float* topk_weights,
-                                       int32_t* topk_ids, orStream_t stream) {
+namespace {
+
+// Checks the router's arguments and fills *p; *fast = the fp32 sigmoid + bias
+// path (fast keys with certificates).
+orError_t router_params(const void* gating, int gating_dtype, int64_t num_tokens, int num_experts,
+                        int num_expert_group, int topk_group, int topk, int renormalize,
+                        float routed_scaling_factor, const float* bias, int scoring_func, float* topk_weights,
+                        int32_t* topk_ids, router::Params* p, bool* fast) {
   const int E = num_experts, G = num_expert_group;
   MCPU_ARG_CHECK(gating_dtype == MCPU_FLOAT32 || gating_dtype == MCPU_BFLOAT16,
                  "grouped_topk: gating must be float32 or bfloat16 (got dtype code %d)", gating_dtype);
@@ -660,36 +685,38 @@ extern "C" orError_t mcpu_grouped_topk(const void* gating, int gating_dtype, int
                  "grouped_topk: topk (%d) exceeds the experts of the selected groups (%d)", topk,
                  topk_group * GS);
   MCPU_ARG_CHECK(!bias || GS >= 2, "grouped_topk: a correction bias needs >= 2 experts per group");
-  if (num_tokens == 0) return orSuccess;
-  MCPU_ARG_CHECK(gating && topk_weights && topk_ids, "grouped_topk: NULL tensor pointer");
+  MCPU_ARG_CHECK(num_tokens == 0 || (gating && topk_weights && topk_ids), "grouped_topk: NULL tensor pointer");
 
-  router::Params p;
-  p.gating = gating;
-  p.bias = bias;
-  p.w_out = topk_weights;
-  p.id_out = topk_ids;
-  p.T = num_tokens;
-  p.E = E;
-  p.G = G;
-  p.GS = GS;
-  p.TG = topk_group;
-  p.K = topk;
-  p.renorm = renormalize ? 1 : 0;
-  p.scale = routed_scaling_factor;
-  p.scoring = scoring_func;
+  p->gating = gating;
+  p->bias = bias;
+  p->w_out = topk_weights;
+  p->id_out = topk_ids;
+  p->T = num_tokens;
+  p->E = E;
+  p->G = G;
+  p->GS = GS;
+  p->TG = topk_group;
+  p->K = topk;
+  p->renorm = renormalize ? 1 : 0;
+  p->scale = routed_scaling_factor;
+  p->scoring = scoring_func;
   int bits = 1;
   while ((1 << bits) < E) ++bits;
-  p.idx_mask = (1u << bits) - 1u;
-  p.idx_quantum = ldexpf(1.0f, bits - 23);
+  p->idx_mask = (1u << bits) - 1u;
+  p->idx_quantum = ldexpf(1.0f, bits - 23);
+  *fast = gating_dtype == MCPU_FLOAT32 && scoring_func == MCPU_SCORING_SIGMOID && bias;
+  return orSuccess;
+}
 
+// One router call on `st` (p checked by router_params).
+orError_t route(const router::Params& p, int gating_dtype, bool fast, cudaStream_t st) {
+  if (p.T == 0) return orSuccess;
   const size_t esz = gating_dtype == MCPU_FLOAT32 ? 4 : 2;
   const size_t vec_elems = 16 / esz;
-  const bool aligned = (reinterpret_cast<uintptr_t>(gating) % 16 == 0) &&
-                       (bias == nullptr || reinterpret_cast<uintptr_t>(bias) % 16 == 0);
-  const bool vec = aligned && (GS % vec_elems == 0) && ((E * esz) % 16 == 0) &&
-                   (bias == nullptr || GS % 4 == 0);
-  const bool fast = gating_dtype == MCPU_FLOAT32 && scoring_func == MCPU_SCORING_SIGMOID && bias;
-  cudaStream_t st = as_cuda(stream);
+  const bool aligned = (reinterpret_cast<uintptr_t>(p.gating) % 16 == 0) &&
+                       (p.bias == nullptr || reinterpret_cast<uintptr_t>(p.bias) % 16 == 0);
+  const bool vec = aligned && (p.GS % vec_elems == 0) && ((p.E * esz) % 16 == 0) &&
+                   (p.bias == nullptr || p.GS % 4 == 0);
   bool handled = false;
   orError_t te = router::launch_hot(p, gating_dtype, fast, st, &handled);
   if (handled || te != orSuccess) return te;
@@ -702,6 +729,111 @@ extern "C" orError_t mcpu_grouped_topk(const void* gating, int gating_dtype, int
     err = router::launch2<__nv_bfloat16, false>(p, vec, st);
   }
   return from_cuda(err, "grouped_topk launch");
+}
+
+// Whether the router + dispatch of p runs as the one fused launch: the
+// four-lane kernel's shape and layout, at most kL4DispatchMaxTiles tiles per
+// CTA over `sms` CTAs.  MCPU_DISPATCH_UNFUSED forces the two-step path.
+bool fused_dispatch_applies(const router::Params& p, bool fast, int sms) {
+  if (!fast || p.T == 0 || !router::use_lanes4_kernel(p)) return false;
+  if (reinterpret_cast<uintptr_t>(p.gating) % 16 != 0) return false;
+  if (p.bias && reinterpret_cast<uintptr_t>(p.bias) % 16 != 0) return false;
+  if (getenv("MCPU_ROUTER_NO_TMA") || getenv("MCPU_DISPATCH_UNFUSED")) return false;
+  if (!driver_entry("cuTensorMapEncodeTiled")) return false;
+  const long long wtiles = (p.T + router::kL4Tokens - 1) / router::kL4Tokens;
+  const long long ctas = (wtiles + router::kL4Warps - 1) / router::kL4Warps;
+  const long long grid = ctas < sms ? ctas : sms;
+  return (wtiles + grid - 1) / grid <= router::kL4DispatchMaxTiles;
+}
+
+// Workspace of the router + dispatch, laid out for `sms` CTAs: the words
+// that start at zero (generation, arrival counts, group sums), then the
+// larger of the fused launch's rows and the two-step path's count matrix.
+orError_t dispatch_workspace_bytes(long long numel, int E, int sms, uint64_t* bytes) {
+  uint64_t moe_bytes = 0;
+  orError_t e = mcpu_moe_align_workspace_bytes(numel, E, &moe_bytes);
+  if (e != orSuccess) return e;
+  const uint64_t head = static_cast<uint64_t>(router::dispatch_rows_word(sms)) * 4;
+  const uint64_t rows = static_cast<uint64_t>(router::dispatch_ws_words(sms)) * 4 - head;
+  *bytes = head + (rows > moe_bytes ? rows : moe_bytes);
+  return orSuccess;
+}
+
+}  // namespace
+
+extern "C" orError_t mcpu_grouped_topk(const void* gating, int gating_dtype, int64_t num_tokens,
+                                       int num_experts, int num_expert_group, int topk_group,
+                                       int topk, int renormalize, float routed_scaling_factor,
+                                       const float* bias, int scoring_func, float* topk_weights,
+                                       int32_t* topk_ids, orStream_t stream) {
+  router::Params p;
+  bool fast = false;
+  orError_t e = router_params(gating, gating_dtype, num_tokens, num_experts, num_expert_group, topk_group, topk,
+                              renormalize, routed_scaling_factor, bias, scoring_func, topk_weights, topk_ids, &p,
+                              &fast);
+  if (e != orSuccess) return e;
+  return route(p, gating_dtype, fast, as_cuda(stream));
+}
+
+extern "C" orError_t mcpu_grouped_topk_moe_align_workspace_bytes(int64_t num_tokens, int num_experts, int topk,
+                                                                 uint64_t* bytes) {
+  MCPU_ARG_CHECK(bytes != nullptr, "grouped_topk_moe_align: NULL output");
+  MCPU_ARG_CHECK(num_tokens >= 0 && topk >= 1 && topk <= 16 && num_tokens * topk < (1LL << 31),
+                 "grouped_topk_moe_align: %lld tokens x topk %d out of range", static_cast<long long>(num_tokens),
+                 topk);
+  return dispatch_workspace_bytes(num_tokens * topk, num_experts, router::device_sms(), bytes);
+}
+
+extern "C" orError_t mcpu_grouped_topk_moe_align(const void* gating, int gating_dtype, int64_t num_tokens,
+                                                 int num_experts, int num_expert_group, int topk_group, int topk,
+                                                 int renormalize, float routed_scaling_factor, const float* bias,
+                                                 int scoring_func, float* topk_weights, int32_t* topk_ids,
+                                                 int block_size, int32_t* sorted_token_ids, int64_t sorted_capacity,
+                                                 int32_t* expert_ids, int64_t expert_ids_capacity,
+                                                 int32_t* num_tokens_post_pad, void* workspace,
+                                                 uint64_t workspace_bytes, orStream_t stream) {
+  router::Params p;
+  bool fast = false;
+  orError_t e = router_params(gating, gating_dtype, num_tokens, num_experts, num_expert_group, topk_group, topk,
+                              renormalize, routed_scaling_factor, bias, scoring_func, topk_weights, topk_ids, &p,
+                              &fast);
+  if (e != orSuccess) return e;
+  MCPU_ARG_CHECK(num_tokens * topk < (1LL << 31), "grouped_topk_moe_align: %lld ids out of range",
+                 static_cast<long long>(num_tokens) * topk);
+  const long long numel = num_tokens * topk;
+  int nchunks = 0;
+  e = moe::check_args(topk_ids, numel, num_experts, block_size, sorted_token_ids, sorted_capacity, expert_ids,
+                      expert_ids_capacity, num_tokens_post_pad, &nchunks);
+  if (e != orSuccess) return e;
+  const int sms = router::device_sms();
+  uint64_t need = 0;
+  e = dispatch_workspace_bytes(numel, num_experts, sms, &need);
+  if (e != orSuccess) return e;
+  MCPU_ARG_CHECK(workspace != nullptr && workspace_bytes >= need && reinterpret_cast<uintptr_t>(workspace) % 16 == 0,
+                 "grouped_topk_moe_align: workspace of %llu bytes (16-byte aligned), %llu needed",
+                 static_cast<unsigned long long>(workspace_bytes), static_cast<unsigned long long>(need));
+  cudaStream_t st = as_cuda(stream);
+  uint32_t* ws = static_cast<uint32_t*>(workspace);
+  if (fused_dispatch_applies(p, fast, sms)) {
+    static router::EncodeTiledFn enc =
+        reinterpret_cast<router::EncodeTiledFn>(driver_entry("cuTensorMapEncodeTiled"));
+    router::Dispatch d;
+    d.sorted = sorted_token_ids;
+    d.sorted_cap = sorted_capacity;
+    d.expert_ids = expert_ids;
+    d.eid_cap = expert_ids_capacity;
+    d.post_pad = num_tokens_post_pad;
+    d.ws = ws;
+    d.bs = block_size;
+    d.max_ctas = sms;
+    return from_cuda(router::launch_lanes4<router::kL4Warps, true>(p, st, enc, &d, sms),
+                     "grouped_topk_moe_align launch");
+  }
+  e = route(p, gating_dtype, fast, st);
+  if (e != orSuccess) return e;
+  return moe::launch(topk_ids, numel, num_experts, block_size, sorted_token_ids, sorted_capacity, expert_ids,
+                     expert_ids_capacity, num_tokens_post_pad,
+                     reinterpret_cast<int32_t*>(ws + router::dispatch_rows_word(sms)), nchunks, st);
 }
 
 orError_t router::read_error(int* flag, bool reset) {

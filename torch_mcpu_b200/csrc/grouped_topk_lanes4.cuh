@@ -31,8 +31,31 @@
 //           over all 256 experts (pair_warp_exact_pick);
 //   weights lane q weighs picks 2q and 2q + 1; the sum over the four lanes
 //           is taken in a fixed order.
+//
+// Expert dispatch in the same launch (kDispatch): the outputs of vLLM's
+// moe_align_block_size (vllm/_custom_ops.py:2247-2264) for the ids the
+// launch writes, with every expert's run in ascending flat index.  Each CTA
+// then routes one contiguous range of tiles, each warp a contiguous run of
+// it (its slice of ids), and:
+//   1. each warp, right after its last tile, counts its slice per expert in
+//      the first 1 KB of its own slot (ids re-read from L2 and kept in
+//      registers);
+//   2. the CTA publishes its expert counts: one row of 16-bit counts, and a
+//      red.add into the sum of its group of 16 CTAs;
+//   3. one grid-wide barrier (cooperative launch; release-add arrival,
+//      bounded acquire wait); meanwhile the CTA sorts its own entries by
+//      expert into a staging buffer in shared memory (stable: per-warp
+//      offsets, then __match_any_sync ranks in index order);
+//   4. expert totals from the group sums, the entries of earlier CTAs from
+//      the earlier groups' sums and this group's earlier rows (at most
+//      groups + 15 loads per expert pair); a scan of the padded totals gives
+//      the run starts;
+//   5. the grid writes the run padding, the tail and the block experts;
+//      each CTA copies every expert's staged segment to its place in one
+//      contiguous run.
 #pragma once
 
+#include "peer.cuh"
 #include "sm100.cuh"
 
 namespace mcpu {
@@ -123,9 +146,360 @@ __device__ __noinline__ void l4_warp_rerank(const float* gx, const float* sbias,
   }
 }
 
+// ---------------------------------------------------------------------------
+// Expert dispatch fused into the router.
+//
+// Workspace, in 32-bit words:
+//   [0]        generation, bumped once per launch (any start value); its
+//              parity picks the arrival count and group sums of the launch
+//   [1], [2]   arrival counts of even / odd generations
+//   [32, ...)  group sums [2 parities][groups][256], one group per 16 CTAs
+//   then       rows [CTAs][128]: each CTA's expert counts, two 16-bit
+//              counts per word
+// Everything before the rows is zero before the first launch; a launch
+// clears the other parity's count and group sums for the next one.
+constexpr int kDispatchHeaderWords = 32;
+constexpr int kDispatchGroup = 16;  // CTAs per group sum
+
+__host__ __device__ constexpr long long dispatch_groups(long long ctas) {
+  return (ctas + kDispatchGroup - 1) / kDispatchGroup;
+}
+// First word of the rows, for a workspace laid out for `max_ctas` CTAs.
+__host__ __device__ constexpr long long dispatch_rows_word(long long max_ctas) {
+  return kDispatchHeaderWords + 2 * dispatch_groups(max_ctas) * kPairE;
+}
+__host__ __device__ constexpr long long dispatch_ws_words(long long max_ctas) {
+  return dispatch_rows_word(max_ctas) + max_ctas * (kPairE / 2);
+}
+
+struct Dispatch {
+  int32_t* sorted;      // sorted_token_ids
+  long long sorted_cap;
+  int32_t* expert_ids;
+  long long eid_cap;
+  int32_t* post_pad;    // num_tokens_post_pad (one int32)
+  uint32_t* ws;
+  int bs;               // block_size
+  int max_ctas;         // CTAs the workspace is laid out for (>= the grid)
+};
+
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void red_release_gpu_add(uint32_t* p, uint32_t v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Counts of the warp's slice of ids [sb, se) per expert into wh[0 .. 255]
+// (the first 1 KB of the warp's own slot, free once its last tile is done),
+// right after the warp's last tile.  ev[] keeps the ids of a slice of at
+// most 128 entries (-1 past its end) for the placement.
+__device__ __forceinline__ void l4_slice_counts(int* wh, const int32_t* ids, long long sb, long long se, int lane,
+                                                int (&ev)[4]) {
+#pragma unroll
+  for (int i = 0; i < kPairE / 32; ++i) wh[i * 32 + lane] = 0;
+  __syncwarp();  // also orders the warp's own id stores before the loads
+  bool badid = false;
+  for (long long b = sb; b < se; b += 128) {
+    int v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const long long i = b + u * 32 + lane;
+      v[u] = i < se ? __ldcg(ids + i) : -1;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (static_cast<unsigned>(v[u]) < static_cast<unsigned>(kPairE))
+        atomicAdd(&wh[v[u]], 1);
+      else if (b + u * 32 + lane < se)
+        badid = true;
+      ev[u] = v[u];
+    }
+  }
+  if (badid) atomicOr(&g_router_error, 4);
+}
+
+// Staging buffer of the CTA's entries, sorted by expert, in the slots after
+// the four scratch slots: the upper 7 KB of each (the first 1 KB holds the
+// slot's warp's slice counts).
+constexpr int kL4StagePerSlot = (kL4Tile - 1024) / 4;  // 1792 entries
+
+__device__ __forceinline__ int* l4_stage_ptr(uint8_t* base, int j) {
+  const int s = j / kL4StagePerSlot;
+  return reinterpret_cast<int*>(base + (4 + s) * kL4Tile + 1024) + (j - s * kL4StagePerSlot);
+}
+
+// One warp's slice placed 32 entries at a time in index order: entry i of
+// expert e goes to out(e) + wh[e] + its rank among the batch's entries of e
+// (__match_any_sync groups equal experts, rank = peers below the lane);
+// wh[e] then advances by the batch's entries of e.  `kept`: the slice's
+// ids are ev[]; else they are re-read from L2.
+template <typename Out>
+__device__ __forceinline__ void l4_place_slice(int* wh, const int32_t* ids, long long sb, long long se,
+                                               bool kept, const int (&ev)[4], int lane, Out out) {
+  const unsigned below = (1u << lane) - 1u;
+  for (long long b0 = sb; b0 < se; b0 += 128) {
+    int v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const long long i = b0 + u * 32 + lane;
+      v[u] = kept ? ev[u] : (i < se ? __ldcg(ids + i) : -1);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const long long b = b0 + u * 32;
+      if (b >= se) break;
+      int e = v[u];
+      if (static_cast<unsigned>(e) >= static_cast<unsigned>(kPairE)) e = -1;
+      const unsigned peers = __match_any_sync(0xFFFFFFFFu, e);
+      const int rank = __popc(peers & below);
+      if (e >= 0) out(e, wh[e] + rank, static_cast<int32_t>(b + lane));
+      __syncwarp();
+      if (e >= 0 && rank == 0) wh[e] += __popc(peers);
+      __syncwarp();
+    }
+  }
+}
+
+// The CTA's part of the dispatch, after every warp's slice counts: publish
+// the CTA's expert counts, sort the CTA's entries by expert in shared
+// memory while the other CTAs arrive, wait for all CTAs (bounded), then
+// copy each expert's segment to its place.  A CTA with more entries than
+// the staging buffer holds places them straight from registers instead.
+// `bad` when one of the CTA's waits ran out: it then only takes part in
+// the barrier.
 template <int NW>
+__device__ __forceinline__ void l4_dispatch(uint8_t* base, int* sflag, const Dispatch& d, const int32_t* ids,
+                                            long long T, long long sb, long long se, const int (&ev)[4],
+                                            bool bad) {
+  constexpr int E = kPairE;
+  constexpr int NT = NW * 32;
+  constexpr int Q = NT / 128;   // groups of 128 threads, each over two experts per thread
+  constexpr int WPQ = NW / Q;   // warps per group
+  constexpr int kStageCap = (NW - 4) * kL4StagePerSlot;
+  static_assert(NT % 128 == 0 && NW % Q == 0 && NT >= E && NW > 4, "dispatch thread layout");
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int p2 = tid & 127, q = tid >> 7;  // experts 2 p2, 2 p2 + 1 of group q
+  // scratch in the first four slots, after their first 1 KB (slice counts)
+  int* psum = reinterpret_cast<int*>(base + 0 * kL4Tile + 1024);  // [Q][E]
+  int* ptot = reinterpret_cast<int*>(base + 1 * kL4Tile + 1024);  // [Q][E]
+  int* pbef = reinterpret_cast<int*>(base + 2 * kL4Tile + 1024);  // [Q][E]
+  int* sstart = reinterpret_cast<int*>(base + 3 * kL4Tile + 1024);  // [E + 1] run starts
+  int* stot = sstart + E + 1;   // [E] expert totals
+  int* sfirst = stot + E;       // [E] this CTA's first slot per expert
+  int* sh = sfirst + E;         // [E] this CTA's entries per expert
+  int* slstart = sh + E;        // [E] their first position in the staging buffer
+  int* wsum = slstart + E;      // [E / 32] scan partials
+  int* wsuml = wsum + E / 32;   // [E / 32] scan partials of the staging positions
+  int* sgen = wsuml + E / 32;
+  uint32_t* ws = d.ws;
+  const long long ngmax = dispatch_groups(d.max_ctas);
+  uint32_t* rows = ws + dispatch_rows_word(d.max_ctas);
+  const int c = blockIdx.x, gi = c / kDispatchGroup;
+  const int ng = static_cast<int>(dispatch_groups(gridDim.x));
+
+  if (tid == 0) *sgen = static_cast<int>(*reinterpret_cast<volatile uint32_t*>(ws));
+  __syncthreads();  // every warp's slice counts are in
+  const uint32_t gen = static_cast<uint32_t>(*sgen);
+  const int par = static_cast<int>(gen & 1u);
+  uint32_t* gs_cur = ws + kDispatchHeaderWords + par * ngmax * E;
+  uint32_t* gs_next = ws + kDispatchHeaderWords + (1 - par) * ngmax * E;
+
+  // 1. the CTA's counts: partial sums over groups of WPQ warps
+  if (!bad) {
+    int2 acc = make_int2(0, 0);
+#pragma unroll
+    for (int j = 0; j < WPQ; ++j) {
+      const int2 v = *reinterpret_cast<const int2*>(base + (q * WPQ + j) * kL4Tile + 8 * p2);
+      acc.x += v.x;
+      acc.y += v.y;
+    }
+    *reinterpret_cast<int2*>(psum + q * E + 2 * p2) = acc;
+  }
+  __syncthreads();
+  int h = 0;
+  if (!bad && tid < E) {
+#pragma unroll
+    for (int j = 0; j < Q; ++j) h += psum[j * E + tid];
+  }
+  // staging positions: exclusive scan of h over the experts (warps 0 .. 7)
+  int hincl = h;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xFFFFFFFFu, hincl, o);
+    if (lane >= o) hincl += v;
+  }
+  if (tid < E && lane == 31) wsuml[warp] = hincl;
+  {
+    const uint32_t hn = __shfl_down_sync(0xFFFFFFFFu, static_cast<uint32_t>(h), 1);
+    if (tid < E && (tid & 1) == 0)
+      rows[static_cast<long long>(c) * (E / 2) + (tid >> 1)] = static_cast<uint32_t>(h) | (hn << 16);
+    if (tid < E && h != 0) atomicAdd(gs_cur + static_cast<long long>(gi) * E + tid, static_cast<uint32_t>(h));
+  }
+  // the next launch's group sums and arrival count start at zero
+  for (long long g = c; g < ngmax; g += gridDim.x)
+    if (tid < E) gs_next[g * E + tid] = 0u;
+  if (c == 0 && tid == 0) ws[1 + (1 - par)] = 0u;
+
+  // 2. arrive (release: the CTA's row and group sum); while the other CTAs
+  // arrive, the per-warp offsets within the CTA and the CTA's entries sorted
+  // by expert into the staging buffer; then wait
+  __syncthreads();
+  if (tid == 0) red_release_gpu_add(ws + 1 + par, 1u);
+  int ncta = 0;  // the CTA's entries
+#pragma unroll
+  for (int w = 0; w < E / 32; ++w) ncta += wsuml[w];
+  const bool staged = ncta <= kStageCap;
+  if (!bad) {
+    int2 run = make_int2(0, 0);
+    for (int j = 0; j < q; ++j) {
+      run.x += psum[j * E + 2 * p2];
+      run.y += psum[j * E + 2 * p2 + 1];
+    }
+#pragma unroll
+    for (int j = 0; j < WPQ; ++j) {
+      int2* w = reinterpret_cast<int2*>(base + (q * WPQ + j) * kL4Tile + 8 * p2);
+      const int2 v = *w;
+      *w = run;
+      run.x += v.x;
+      run.y += v.y;
+    }
+    if (tid < E) {
+      int off = 0;
+      for (int w = 0; w < warp; ++w) off += wsuml[w];
+      sh[tid] = h;
+      slstart[tid] = off + hincl - h;
+    }
+  }
+  __syncthreads();
+  int* wh = reinterpret_cast<int*>(base + warp * kL4Tile);
+  const bool kept = se - sb <= 128;
+  if (!bad && staged)
+    l4_place_slice(wh, ids, sb, se, kept, ev, lane,
+                   [&](int e, int pos, int32_t i) { *l4_stage_ptr(base, slstart[e] + pos) = i; });
+  if (tid == 0) {
+    bool ok = false;
+    const unsigned long long t0 = peer::globaltimer();
+    for (uint32_t i = 0; i < peer::kWaitPolls; ++i) {
+      if (ld_acquire_gpu(ws + 1 + par) == gridDim.x) {
+        ok = true;
+        break;
+      }
+      if ((i & 31u) == 31u && peer::globaltimer() - t0 > peer::kWaitNs) break;
+    }
+    *sflag = ok ? 1 : 0;
+  }
+  __syncthreads();
+  if (*sflag == 0) {
+    if (tid == 0) atomicOr(&g_router_error, 2);
+    return;
+  }
+  if (c == 0 && tid == 0) ws[0] = gen + 1u;  // every CTA read the generation before it arrived
+  if (bad) return;
+
+  // 3. expert totals (all group sums) and the entries of earlier CTAs (the
+  // group sums of earlier groups, the rows of earlier CTAs of this group)
+  {
+    uint32_t tl = 0, th = 0, bl = 0, bh = 0;
+#pragma unroll 2
+    for (int g = q; g < ng; g += Q) {
+      const uint2 v = __ldcg(reinterpret_cast<const uint2*>(gs_cur + static_cast<long long>(g) * E) + p2);
+      tl += v.x;
+      th += v.y;
+      if (g < gi) {
+        bl += v.x;
+        bh += v.y;
+      }
+    }
+    const int r0 = gi * kDispatchGroup;
+#pragma unroll 3
+    for (int r = r0 + q; r < c; r += Q) {
+      const uint32_t v = __ldcg(rows + static_cast<long long>(r) * (E / 2) + p2);
+      bl += v & 0xFFFFu;
+      bh += v >> 16;
+    }
+    *reinterpret_cast<int2*>(ptot + q * E + 2 * p2) = make_int2(static_cast<int>(tl), static_cast<int>(th));
+    *reinterpret_cast<int2*>(pbef + q * E + 2 * p2) = make_int2(static_cast<int>(bl), static_cast<int>(bh));
+  }
+  __syncthreads();
+  int tot = 0, bef = 0;
+  if (tid < E) {
+#pragma unroll
+    for (int j = 0; j < Q; ++j) {
+      tot += ptot[j * E + tid];
+      bef += pbef[j * E + tid];
+    }
+  }
+  const int padded = tid < E ? (tot + d.bs - 1) / d.bs * d.bs : 0;
+  int incl = padded;  // inclusive scan over the experts (warps 0 .. E/32 - 1)
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (tid < E && lane == 31) wsum[warp] = incl;
+  __syncthreads();
+  if (tid < E) {
+    int off = 0;
+    for (int w = 0; w < warp; ++w) off += wsum[w];
+    const int start = off + incl - padded;
+    sstart[tid] = start;
+    stot[tid] = tot;
+    sfirst[tid] = start + bef;
+    if (tid == E - 1) sstart[E] = off + incl;
+  }
+  __syncthreads();
+  const int end = sstart[E];
+  if (c == 0 && tid == 0) *d.post_pad = end;
+
+  // 4. shared by the grid: run padding (expert e by CTA e % grid), the slots
+  // after the last run and the expert of every block
+  const int32_t numel = static_cast<int32_t>(T * kPairKMax);
+  for (int e = c; e < E; e += gridDim.x) {
+    const int from = sstart[e] + stot[e], to = sstart[e + 1];
+    for (int j = from + tid; j < to; j += NT) d.sorted[j] = numel;
+  }
+  const long long gtid = static_cast<long long>(c) * NT + tid;
+  const long long gthreads = static_cast<long long>(gridDim.x) * NT;
+  for (long long j = end + gtid; j < d.sorted_cap; j += gthreads) d.sorted[j] = numel;
+  for (long long b = gtid; b < d.eid_cap; b += gthreads) {
+    const long long slot = b * d.bs;
+    int ex = -1;
+    if (slot < end) {
+      int lo = 0, hi = E - 1;  // largest expert whose run starts at or before the slot
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (sstart[mid] <= slot)
+          lo = mid;
+        else
+          hi = mid - 1;
+      }
+      ex = lo;
+    }
+    d.expert_ids[b] = ex;
+  }
+
+  // 5. the CTA's entries to their places: each expert's staged segment in
+  // one contiguous copy (warp w takes experts w, w + NW, ...), or, when they
+  // did not fit the staging buffer, each warp's slice straight from its ids
+  if (staged) {
+    for (int e = warp; e < E; e += NW) {
+      const int n = sh[e], src = slstart[e], dst = sfirst[e];
+      for (int k = lane; k < n; k += 32) d.sorted[dst + k] = *l4_stage_ptr(base, src + k);
+    }
+  } else {
+    l4_place_slice(wh, ids, sb, se, kept, ev, lane,
+                   [&](int e, int pos, int32_t i) { d.sorted[sfirst[e] + pos] = i; });
+  }
+}
+
+template <int NW, bool kDispatch>
 __global__ void __launch_bounds__(NW * 32, 1) grouped_topk_lanes4_kernel(
-    const __grid_constant__ CUtensorMap tm, const Params p, const long long wtiles, const int vec_out) {
+    const __grid_constant__ CUtensorMap tm, const Params p, const long long wtiles, const int vec_out,
+    const Dispatch d) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t ra = sm100::smem_u32(smem_raw);
   uint8_t* base = smem_raw + ((1024 - (ra & 1023)) & 1023);
@@ -142,8 +516,21 @@ __global__ void __launch_bounds__(NW * 32, 1) grouped_topk_lanes4_kernel(
   const int q = lane >> 3;        // quarter: groups 2q, 2q + 1
   const int rowoff = t * 128;     // the token's row in every group box
   const int x7 = t << 4;          // its 128-byte swizzle (row t of the atom)
-  const long long gw = static_cast<long long>(blockIdx.x) * NW + warp;
-  const long long nw = static_cast<long long>(gridDim.x) * NW;
+  // tiles tfirst, tfirst + tstep, ... below tend: round-robin over the grid,
+  // or (dispatch) a contiguous run of the CTA's contiguous range [c0, c1)
+  long long tfirst, tstep, tend;
+  if constexpr (kDispatch) {
+    const long long c0 = static_cast<long long>(blockIdx.x) * wtiles / gridDim.x;
+    const long long c1 = static_cast<long long>(blockIdx.x + 1) * wtiles / gridDim.x;
+    const long long tpw = (c1 - c0 + NW - 1) / NW;
+    tfirst = c0 + warp * tpw;
+    tstep = 1;
+    tend = tfirst + tpw < c1 ? tfirst + tpw : c1;
+  } else {
+    tfirst = static_cast<long long>(blockIdx.x) * NW + warp;
+    tstep = static_cast<long long>(gridDim.x) * NW;
+    tend = wtiles;
+  }
   const float* gating = static_cast<const float*>(p.gating);
 
   auto issue = [&](long long wt) {
@@ -159,15 +546,15 @@ __global__ void __launch_bounds__(NW * 32, 1) grouped_topk_lanes4_kernel(
     sm100::fence_barrier_init();
   }
   __syncwarp();
-  if (gw < wtiles) issue(gw);
+  if (tfirst < tend) issue(tfirst);
   for (int i = threadIdx.x; i < kPairE; i += blockDim.x) sbias[i] = p.bias[i];
-  __syncthreads();  // the only CTA-wide barrier: bias staged
+  __syncthreads();  // the only CTA-wide barrier of the routing loop: bias staged
 
   long long it = 0;
-  bool inflight = gw < wtiles;
+  bool inflight = tfirst < tend;
   for (;; ++it) {
-    const long long wt = gw + it * nw;
-    if (wt >= wtiles) break;
+    const long long wt = tfirst + it * tstep;
+    if (wt >= tend) break;
     const bool ok = sm100::mbar_wait(full, static_cast<uint32_t>(it & 1), abort_flag);
     if (!__all_sync(0xFFFFFFFFu, ok)) break;
     inflight = false;
@@ -321,9 +708,9 @@ __global__ void __launch_bounds__(NW * 32, 1) grouped_topk_lanes4_kernel(
     __syncwarp();
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     {
-      const long long nt = wt + nw;
-      if (nt < wtiles) issue(nt);
-      inflight = nt < wtiles;
+      const long long nt = wt + tstep;
+      if (nt < tend) issue(nt);
+      inflight = nt < tend;
     }
 
     // ---- weights; the sum over the four lanes in a fixed order
@@ -394,6 +781,19 @@ __global__ void __launch_bounds__(NW * 32, 1) grouped_topk_lanes4_kernel(
            ++n) {
       }
     }
+  }
+  if constexpr (kDispatch) {
+    // the warp's slice of ids: its tokens [tfirst * 8, min(tend * 8, T))
+    const long long sb = tfirst * (kL4Tokens * kPairKMax);
+    long long se = tend * (kL4Tokens * kPairKMax);
+    if (se > p.T * kPairKMax) se = p.T * kPairKMax;
+    if (se < sb) se = sb;
+    const bool wbad = __shfl_sync(0xFFFFFFFFu, lane == 0 ? *abort_flag : 0, 0) != 0;
+    int ev[4] = {-1, -1, -1, -1};
+    if (!wbad) l4_slice_counts(reinterpret_cast<int*>(tb), p.id_out, sb, se, lane, ev);
+    const bool bad = __syncthreads_or(wbad) != 0;
+    int* sync_flag = reinterpret_cast<int*>(base + L.bar_off + 12);  // spare word of warp 0's barrier slot
+    l4_dispatch<NW>(base, sync_flag, d, p.id_out, p.T, sb, se, ev, bad);
   }
 }
 

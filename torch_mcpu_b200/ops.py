@@ -212,6 +212,78 @@ def moe_align_block_size(topk_ids: torch.Tensor, block_size: int, num_experts: i
     return sorted_ids, expert_ids, post_pad
 
 
+_DISPATCH_WS: dict = {}
+
+
+def _dispatch_workspace(dev: torch.device, stream: int, nbytes: int) -> torch.Tensor:
+    """Zero-filled workspace of grouped_topk_moe_align, one per (device,
+    stream): each call leaves it ready for the next, so it is reused as is."""
+    key = (dev.index, stream)
+    ws = _DISPATCH_WS.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+        _DISPATCH_WS[key] = ws
+    return ws
+
+
+def grouped_topk_moe_align(
+    hidden_states: torch.Tensor,
+    gating_output: torch.Tensor,
+    topk: int,
+    renormalize: bool,
+    num_expert_group: int,
+    topk_group: int,
+    scoring_func: str = "softmax",
+    routed_scaling_factor: float = 1.0,
+    e_score_correction_bias: torch.Tensor | None = None,
+    block_size: int = 64,
+):
+    """grouped_topk followed by moe_align_block_size on its ids, as vLLM's
+    fused MoE runs them; one launch for DeepSeek-V3's router shape.  Returns
+    (topk_weights, topk_ids, sorted_token_ids, expert_ids, num_tokens_post_pad),
+    bit-identical to the two ops called one after the other."""
+    import ctypes
+
+    if hidden_states.size(0) != gating_output.size(0):
+        raise AssertionError("Number of tokens mismatch")
+    if scoring_func not in _SCORING:
+        raise ValueError(f"Unsupported scoring function: {scoring_func}")
+    _require_device(gating_output, "gating_output")
+    if gating_output.dim() != 2 or gating_output.dtype not in _DTYPES:
+        raise RuntimeError("grouped_topk_moe_align: gating_output must be a float32 or bfloat16 "
+                           "[num_tokens, num_experts] tensor")
+    g = gating_output.contiguous()
+    T, E = g.shape
+    bias = None
+    if e_score_correction_bias is not None:
+        _require_device(e_score_correction_bias, "e_score_correction_bias")
+        if e_score_correction_bias.numel() != E:
+            raise RuntimeError("grouped_topk: e_score_correction_bias must have num_experts elements")
+        bias = e_score_correction_bias.to(torch.float32).contiguous()
+    dev = g.device
+    numel = T * topk
+    cap = min(numel + E * (block_size - 1), numel * block_size)
+    nblocks = -(-cap // block_size)
+    w = torch.empty(T, topk, dtype=torch.float32, device=dev)
+    ids = torch.empty(T, topk, dtype=torch.int32, device=dev)
+    sorted_ids = torch.empty(max(cap, 1), dtype=torch.int32, device=dev)[:cap]
+    expert_ids = torch.empty(max(nblocks, 1), dtype=torch.int32, device=dev)[:nblocks]
+    post_pad = torch.empty(1, dtype=torch.int32, device=dev)
+    lib = _lib.load()
+    nb = ctypes.c_uint64()
+    _lib.check(lib.mcpu_grouped_topk_moe_align_workspace_bytes(T, E, topk, ctypes.byref(nb)),
+               "grouped_topk_moe_align")
+    stream = _stream_handle(dev)
+    ws = _dispatch_workspace(dev, stream, nb.value)
+    _lib.check(lib.mcpu_grouped_topk_moe_align(
+        g.data_ptr(), _DTYPES[g.dtype], T, E, num_expert_group, topk_group, topk, int(bool(renormalize)),
+        float(routed_scaling_factor), None if bias is None else bias.data_ptr(), _SCORING[scoring_func],
+        w.data_ptr(), ids.data_ptr(), block_size, sorted_ids.data_ptr(), sorted_ids.numel(),
+        expert_ids.data_ptr(), expert_ids.numel(), post_pad.data_ptr(), ws.data_ptr(), ws.numel(), stream),
+        "grouped_topk_moe_align")
+    return w, ids, sorted_ids, expert_ids, post_pad
+
+
 def device_error(reset: bool = False) -> int:
     """1 if a kernel gave up on a bounded wait since the last reset."""
     import ctypes
