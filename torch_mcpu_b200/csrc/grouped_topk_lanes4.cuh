@@ -45,14 +45,14 @@
 //   3. one grid-wide barrier (cooperative launch; release-add arrival,
 //      bounded acquire wait); meanwhile the CTA sorts its own entries by
 //      expert into a staging buffer in shared memory (stable: per-warp
-//      offsets, then __match_any_sync ranks in index order);
+//      offsets, then each warp's slice one token a step in index order);
 //   4. expert totals from the group sums, the entries of earlier CTAs from
 //      the earlier groups' sums and this group's earlier rows (at most
 //      groups + 15 loads per expert pair); a scan of the padded totals gives
 //      the run starts;
 //   5. the grid writes the run padding, the tail and the block experts;
-//      each CTA copies every expert's staged segment to its place in one
-//      contiguous run.
+//      each CTA copies its sorted entries out, every expert's entries in
+//      one contiguous run.
 #pragma once
 
 #include "peer.cuh"
@@ -232,15 +232,16 @@ __device__ __forceinline__ int* l4_stage_ptr(uint8_t* base, int j) {
   return reinterpret_cast<int*>(base + (4 + s) * kL4Tile + 1024) + (j - s * kL4StagePerSlot);
 }
 
-// One warp's slice placed 32 entries at a time in index order: entry i of
-// expert e goes to out(e) + wh[e] + its rank among the batch's entries of e
-// (__match_any_sync groups equal experts, rank = peers below the lane);
-// wh[e] then advances by the batch's entries of e.  `kept`: the slice's
-// ids are ev[]; else they are re-read from L2.
+// One warp's slice placed in index order, one token (8 entries, 8 lanes) a
+// step: entry i of expert e goes to out(e, wh[e], i) and wh[e] advances
+// (shared-memory atomic; a token's 8 experts are distinct, and where they
+// are not the atomic still gives every entry its own place).  A batch of
+// 32 entries holds 4 whole tokens (slices start on a tile).  `kept`: the
+// slice's ids are ev[]; else they are re-read from L2.
 template <typename Out>
-__device__ __forceinline__ void l4_place_slice(int* wh, const int32_t* ids, long long sb, long long se,
-                                               bool kept, const int (&ev)[4], int lane, Out out) {
-  const unsigned below = (1u << lane) - 1u;
+__device__ __forceinline__ void l4_place_tokens(int* wh, const int32_t* ids, long long sb, long long se,
+                                                bool kept, const int (&ev)[4], int lane, Out out) {
+  const int tok = lane >> 3;
   for (long long b0 = sb; b0 < se; b0 += 128) {
     int v[4];
 #pragma unroll
@@ -252,23 +253,23 @@ __device__ __forceinline__ void l4_place_slice(int* wh, const int32_t* ids, long
     for (int u = 0; u < 4; ++u) {
       const long long b = b0 + u * 32;
       if (b >= se) break;
-      int e = v[u];
-      if (static_cast<unsigned>(e) >= static_cast<unsigned>(kPairE)) e = -1;
-      const unsigned peers = __match_any_sync(0xFFFFFFFFu, e);
-      const int rank = __popc(peers & below);
-      if (e >= 0) out(e, wh[e] + rank, static_cast<int32_t>(b + lane));
-      __syncwarp();
-      if (e >= 0 && rank == 0) wh[e] += __popc(peers);
-      __syncwarp();
+      const int e = v[u];
+      const bool ok = b + lane < se && static_cast<unsigned>(e) < static_cast<unsigned>(kPairE);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (tok == j && ok) out(e, atomicAdd(&wh[e], 1), static_cast<int32_t>(b + lane));
+        __syncwarp();
+      }
     }
   }
 }
 
 // The CTA's part of the dispatch, after every warp's slice counts: publish
 // the CTA's expert counts, sort the CTA's entries by expert in shared
-// memory while the other CTAs arrive, wait for all CTAs (bounded), then
-// copy each expert's segment to its place.  A CTA with more entries than
-// the staging buffer holds places them straight from registers instead.
+// memory (each as index << 8 | expert) while the other CTAs arrive, wait for
+// all CTAs (bounded), then copy the sorted entries to their places.  When
+// the entries do not fit the staging buffer, or an index needs more than 24
+// bits, each warp places its slice straight into the output instead.
 // `bad` when one of the CTA's waits ran out: it then only takes part in
 // the barrier.
 template <int NW>
@@ -290,8 +291,7 @@ __device__ __forceinline__ void l4_dispatch(uint8_t* base, int* sflag, const Dis
   int* sstart = reinterpret_cast<int*>(base + 3 * kL4Tile + 1024);  // [E + 1] run starts
   int* stot = sstart + E + 1;   // [E] expert totals
   int* sfirst = stot + E;       // [E] this CTA's first slot per expert
-  int* sh = sfirst + E;         // [E] this CTA's entries per expert
-  int* slstart = sh + E;        // [E] their first position in the staging buffer
+  int* slstart = sfirst + E;    // [E] its first position in the staging buffer
   int* wsum = slstart + E;      // [E / 32] scan partials
   int* wsuml = wsum + E / 32;   // [E / 32] scan partials of the staging positions
   int* sgen = wsuml + E / 32;
@@ -352,7 +352,7 @@ __device__ __forceinline__ void l4_dispatch(uint8_t* base, int* sflag, const Dis
   int ncta = 0;  // the CTA's entries
 #pragma unroll
   for (int w = 0; w < E / 32; ++w) ncta += wsuml[w];
-  const bool staged = ncta <= kStageCap;
+  const bool staged = ncta <= kStageCap && T * kPairKMax <= (1LL << 24);
   if (!bad) {
     int2 run = make_int2(0, 0);
     for (int j = 0; j < q; ++j) {
@@ -370,7 +370,6 @@ __device__ __forceinline__ void l4_dispatch(uint8_t* base, int* sflag, const Dis
     if (tid < E) {
       int off = 0;
       for (int w = 0; w < warp; ++w) off += wsuml[w];
-      sh[tid] = h;
       slstart[tid] = off + hincl - h;
     }
   }
@@ -378,8 +377,10 @@ __device__ __forceinline__ void l4_dispatch(uint8_t* base, int* sflag, const Dis
   int* wh = reinterpret_cast<int*>(base + warp * kL4Tile);
   const bool kept = se - sb <= 128;
   if (!bad && staged)
-    l4_place_slice(wh, ids, sb, se, kept, ev, lane,
-                   [&](int e, int pos, int32_t i) { *l4_stage_ptr(base, slstart[e] + pos) = i; });
+    l4_place_tokens(wh, ids, sb, se, kept, ev, lane,
+                    [&](int e, int pos, int32_t i) {
+                      *l4_stage_ptr(base, slstart[e] + pos) = static_cast<int>((static_cast<uint32_t>(i) << 8) | e);
+                    });
   if (tid == 0) {
     bool ok = false;
     const unsigned long long t0 = peer::globaltimer();
@@ -482,17 +483,18 @@ __device__ __forceinline__ void l4_dispatch(uint8_t* base, int* sflag, const Dis
     d.expert_ids[b] = ex;
   }
 
-  // 5. the CTA's entries to their places: each expert's staged segment in
-  // one contiguous copy (warp w takes experts w, w + NW, ...), or, when they
-  // did not fit the staging buffer, each warp's slice straight from its ids
+  // 5. the CTA's entries to their places: staged entry j of expert e goes
+  // to sfirst[e] + (j - slstart[e]), so each expert's entries land in one
+  // contiguous run; or each warp's slice straight from its ids
   if (staged) {
-    for (int e = warp; e < E; e += NW) {
-      const int n = sh[e], src = slstart[e], dst = sfirst[e];
-      for (int k = lane; k < n; k += 32) d.sorted[dst + k] = *l4_stage_ptr(base, src + k);
+    for (int j = tid; j < ncta; j += NT) {
+      const uint32_t v = static_cast<uint32_t>(*l4_stage_ptr(base, j));
+      const int e = static_cast<int>(v & 255u);
+      d.sorted[sfirst[e] + (j - slstart[e])] = static_cast<int32_t>(v >> 8);
     }
   } else {
-    l4_place_slice(wh, ids, sb, se, kept, ev, lane,
-                   [&](int e, int pos, int32_t i) { d.sorted[sfirst[e] + pos] = i; });
+    l4_place_tokens(wh, ids, sb, se, kept, ev, lane,
+                    [&](int e, int pos, int32_t i) { d.sorted[sfirst[e] + pos] = i; });
   }
 }
 
