@@ -44,8 +44,9 @@
 //      red.add into the sum of its group of 16 CTAs;
 //   3. one grid-wide barrier (cooperative launch; release-add arrival,
 //      bounded acquire wait); meanwhile the CTA sorts its own entries by
-//      expert into a staging buffer in shared memory (stable: per-warp
-//      offsets, then each warp's slice one token a step in index order);
+//      expert into a staging buffer in shared memory: per-warp offsets plus
+//      the ranks the counting pass's atomics returned (one token at a time,
+//      so in index order);
 //   4. expert totals from the group sums, the entries of earlier CTAs from
 //      the earlier groups' sums and this group's earlier rows (at most
 //      groups + 15 loads per expert pair); a scan of the padded totals gives
@@ -183,6 +184,15 @@ struct Dispatch {
   int max_ctas;         // CTAs the workspace is laid out for (>= the grid)
 };
 
+// Thread `first + k` loads word k * 16384 of [p, p + n) (one per 64 KB), so
+// that the buffer's address translations are cached before it is written:
+// the logits streamed while routing evict them.
+__device__ __forceinline__ void l4_touch(const int32_t* p, long long n, int tid, int first) {
+  const long long k = tid - first;
+  if (k >= 0 && k < 64 && k * 16384 < n)
+    asm volatile("{\n .reg .u32 t;\n ld.global.cg.u32 t, [%0];\n}" ::"l"(p + k * 16384) : "memory");
+}
+
 __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
   uint32_t v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -195,10 +205,12 @@ __device__ __forceinline__ void red_release_gpu_add(uint32_t* p, uint32_t v) {
 
 // Counts of the warp's slice of ids [sb, se) per expert into wh[0 .. 255]
 // (the first 1 KB of the warp's own slot, free once its last tile is done),
-// right after the warp's last tile.  ev[] keeps the ids of a slice of at
-// most 128 entries (-1 past its end) for the placement.
+// right after the warp's last tile.  The atomics go one token (8 lanes) at
+// a time, so for a slice of at most 128 entries rk[] holds each entry's
+// count of earlier entries of its expert in the slice (a token's experts
+// are distinct); ev[] keeps the ids (-1 past the slice's end).
 __device__ __forceinline__ void l4_slice_counts(int* wh, const int32_t* ids, long long sb, long long se, int lane,
-                                                int (&ev)[4]) {
+                                                int (&ev)[4], int (&rk)[4]) {
 #pragma unroll
   for (int i = 0; i < kPairE / 32; ++i) wh[i * 32 + lane] = 0;
   __syncwarp();  // also orders the warp's own id stores before the loads
@@ -212,11 +224,16 @@ __device__ __forceinline__ void l4_slice_counts(int* wh, const int32_t* ids, lon
     }
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
-      if (static_cast<unsigned>(v[u]) < static_cast<unsigned>(kPairE))
-        atomicAdd(&wh[v[u]], 1);
-      else if (b + u * 32 + lane < se)
-        badid = true;
+      const bool ok = static_cast<unsigned>(v[u]) < static_cast<unsigned>(kPairE);
+      if (!ok && b + u * 32 + lane < se) badid = true;
+      int r = 0;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {  // token j of the batch: lanes 8j .. 8j + 7
+        if ((lane >> 3) == j && ok) r = atomicAdd(&wh[v[u]], 1);
+        __syncwarp();
+      }
       ev[u] = v[u];
+      rk[u] = r;
     }
   }
   if (badid) atomicOr(&g_router_error, 4);
@@ -275,7 +292,7 @@ __device__ __forceinline__ void l4_place_tokens(int* wh, const int32_t* ids, lon
 template <int NW>
 __device__ __forceinline__ void l4_dispatch(uint8_t* base, int* sflag, const Dispatch& d, const int32_t* ids,
                                             long long T, long long sb, long long se, const int (&ev)[4],
-                                            bool bad) {
+                                            const int (&rk)[4], const uint32_t* gen_smem, bool bad) {
   constexpr int E = kPairE;
   constexpr int NT = NW * 32;
   constexpr int Q = NT / 128;   // groups of 128 threads, each over two experts per thread
@@ -294,16 +311,14 @@ __device__ __forceinline__ void l4_dispatch(uint8_t* base, int* sflag, const Dis
   int* slstart = sfirst + E;    // [E] its first position in the staging buffer
   int* wsum = slstart + E;      // [E / 32] scan partials
   int* wsuml = wsum + E / 32;   // [E / 32] scan partials of the staging positions
-  int* sgen = wsuml + E / 32;
   uint32_t* ws = d.ws;
   const long long ngmax = dispatch_groups(d.max_ctas);
   uint32_t* rows = ws + dispatch_rows_word(d.max_ctas);
   const int c = blockIdx.x, gi = c / kDispatchGroup;
   const int ng = static_cast<int>(dispatch_groups(gridDim.x));
 
-  if (tid == 0) *sgen = static_cast<int>(*reinterpret_cast<volatile uint32_t*>(ws));
   __syncthreads();  // every warp's slice counts are in
-  const uint32_t gen = static_cast<uint32_t>(*sgen);
+  const uint32_t gen = *gen_smem;
   const int par = static_cast<int>(gen & 1u);
   uint32_t* gs_cur = ws + kDispatchHeaderWords + par * ngmax * E;
   uint32_t* gs_next = ws + kDispatchHeaderWords + (1 - par) * ngmax * E;
@@ -333,31 +348,41 @@ __device__ __forceinline__ void l4_dispatch(uint8_t* base, int* sflag, const Dis
     if (lane >= o) hincl += v;
   }
   if (tid < E && lane == 31) wsuml[warp] = hincl;
+  if (tid < E) slstart[tid] = hincl - h;  // within its group of 32 experts until the offsets below
   {
     const uint32_t hn = __shfl_down_sync(0xFFFFFFFFu, static_cast<uint32_t>(h), 1);
     if (tid < E && (tid & 1) == 0)
       rows[static_cast<long long>(c) * (E / 2) + (tid >> 1)] = static_cast<uint32_t>(h) | (hn << 16);
     if (tid < E && h != 0) atomicAdd(gs_cur + static_cast<long long>(gi) * E + tid, static_cast<uint32_t>(h));
   }
-  // the next launch's group sums and arrival count start at zero
-  for (long long g = c; g < ngmax; g += gridDim.x)
-    if (tid < E) gs_next[g * E + tid] = 0u;
-  if (c == 0 && tid == 0) ws[1 + (1 - par)] = 0u;
-
   // 2. arrive (release: the CTA's row and group sum); while the other CTAs
   // arrive, the per-warp offsets within the CTA and the CTA's entries sorted
   // by expert into the staging buffer; then wait
   __syncthreads();
   if (tid == 0) red_release_gpu_add(ws + 1 + par, 1u);
+  // the next launch's group sums and arrival count start at zero
+  for (long long g = c; g < ngmax; g += gridDim.x)
+    if (tid < E) gs_next[g * E + tid] = 0u;
+  if (c == 0 && tid == 0) ws[1 + (1 - par)] = 0u;
+  l4_touch(d.sorted, d.sorted_cap, tid, 0);
+  l4_touch(d.expert_ids, d.eid_cap, tid, 64);
   int ncta = 0;  // the CTA's entries
 #pragma unroll
   for (int w = 0; w < E / 32; ++w) ncta += wsuml[w];
   const bool staged = ncta <= kStageCap && T * kPairKMax <= (1LL << 24);
   if (!bad) {
+    // per-warp offsets of experts 2 p2, 2 p2 + 1 within the CTA; staged,
+    // plus the experts' first staging positions
     int2 run = make_int2(0, 0);
     for (int j = 0; j < q; ++j) {
       run.x += psum[j * E + 2 * p2];
       run.y += psum[j * E + 2 * p2 + 1];
+    }
+    if (staged) {
+      int off = 0;
+      for (int w = 0; w < (2 * p2) / 32; ++w) off += wsuml[w];
+      run.x += off + slstart[2 * p2];  // (slstart is 4-byte aligned only)
+      run.y += off + slstart[2 * p2 + 1];
     }
 #pragma unroll
     for (int j = 0; j < WPQ; ++j) {
@@ -367,20 +392,31 @@ __device__ __forceinline__ void l4_dispatch(uint8_t* base, int* sflag, const Dis
       run.x += v.x;
       run.y += v.y;
     }
-    if (tid < E) {
-      int off = 0;
-      for (int w = 0; w < warp; ++w) off += wsuml[w];
-      slstart[tid] = off + hincl - h;
-    }
   }
   __syncthreads();
+  if (!bad && tid < E) {  // each expert's first staging position, for the copy-out
+    int off = 0;
+    for (int w = 0; w < warp; ++w) off += wsuml[w];
+    slstart[tid] += off;
+  }
   int* wh = reinterpret_cast<int*>(base + warp * kL4Tile);
   const bool kept = se - sb <= 128;
-  if (!bad && staged)
-    l4_place_tokens(wh, ids, sb, se, kept, ev, lane,
-                    [&](int e, int pos, int32_t i) {
-                      *l4_stage_ptr(base, slstart[e] + pos) = static_cast<int>((static_cast<uint32_t>(i) << 8) | e);
-                    });
+  if (!bad && staged) {  // wh[e]: this warp's first staging position of expert e
+    if (kept) {  // positions from the counting pass's ranks, all at once
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const long long i = sb + u * 32 + lane;
+        const int e = ev[u];
+        if (i < se && static_cast<unsigned>(e) < static_cast<unsigned>(E))
+          *l4_stage_ptr(base, wh[e] + rk[u]) =
+              static_cast<int>((static_cast<uint32_t>(i) << 8) | static_cast<uint32_t>(e));
+      }
+    } else {
+      l4_place_tokens(wh, ids, sb, se, kept, ev, lane, [&](int e, int pos, int32_t i) {
+        *l4_stage_ptr(base, pos) = static_cast<int>((static_cast<uint32_t>(i) << 8) | e);
+      });
+    }
+  }
   if (tid == 0) {
     bool ok = false;
     const unsigned long long t0 = peer::globaltimer();
@@ -458,30 +494,17 @@ __device__ __forceinline__ void l4_dispatch(uint8_t* base, int* sflag, const Dis
 
   // 4. shared by the grid: run padding (expert e by CTA e % grid), the slots
   // after the last run and the expert of every block
+  // (runs start on block boundaries: every padded total is a multiple of bs)
   const int32_t numel = static_cast<int32_t>(T * kPairKMax);
   for (int e = c; e < E; e += gridDim.x) {
     const int from = sstart[e] + stot[e], to = sstart[e + 1];
     for (int j = from + tid; j < to; j += NT) d.sorted[j] = numel;
+    for (int b = sstart[e] / d.bs + tid; b < to / d.bs; b += NT) d.expert_ids[b] = e;
   }
   const long long gtid = static_cast<long long>(c) * NT + tid;
   const long long gthreads = static_cast<long long>(gridDim.x) * NT;
   for (long long j = end + gtid; j < d.sorted_cap; j += gthreads) d.sorted[j] = numel;
-  for (long long b = gtid; b < d.eid_cap; b += gthreads) {
-    const long long slot = b * d.bs;
-    int ex = -1;
-    if (slot < end) {
-      int lo = 0, hi = E - 1;  // largest expert whose run starts at or before the slot
-      while (lo < hi) {
-        const int mid = (lo + hi + 1) >> 1;
-        if (sstart[mid] <= slot)
-          lo = mid;
-        else
-          hi = mid - 1;
-      }
-      ex = lo;
-    }
-    d.expert_ids[b] = ex;
-  }
+  for (long long b = end / d.bs + gtid; b < d.eid_cap; b += gthreads) d.expert_ids[b] = -1;
 
   // 5. the CTA's entries to their places: staged entry j of expert e goes
   // to sfirst[e] + (j - slstart[e]), so each expert's entries land in one
@@ -546,6 +569,12 @@ __global__ void __launch_bounds__(NW * 32, 1) grouped_topk_lanes4_kernel(
     sm100::mbar_init(full, 1);
     *abort_flag = 0;
     sm100::fence_barrier_init();
+  }
+  if constexpr (kDispatch) {
+    // the dispatch's generation, fixed until every CTA of this launch has
+    // arrived at its barrier: kept in the spare word of warp 1's barrier slot
+    if (threadIdx.x == 0)
+      *reinterpret_cast<uint32_t*>(base + L.bar_off + 16 + 12) = *reinterpret_cast<volatile uint32_t*>(d.ws);
   }
   __syncwarp();
   if (tfirst < tend) issue(tfirst);
@@ -791,11 +820,13 @@ __global__ void __launch_bounds__(NW * 32, 1) grouped_topk_lanes4_kernel(
     if (se > p.T * kPairKMax) se = p.T * kPairKMax;
     if (se < sb) se = sb;
     const bool wbad = __shfl_sync(0xFFFFFFFFu, lane == 0 ? *abort_flag : 0, 0) != 0;
-    int ev[4] = {-1, -1, -1, -1};
-    if (!wbad) l4_slice_counts(reinterpret_cast<int*>(tb), p.id_out, sb, se, lane, ev);
+    if (lane == 0) l4_touch(reinterpret_cast<const int32_t*>(d.ws), dispatch_ws_words(d.max_ctas), 0, 0);
+    int ev[4] = {-1, -1, -1, -1}, rk[4] = {0, 0, 0, 0};
+    if (!wbad) l4_slice_counts(reinterpret_cast<int*>(tb), p.id_out, sb, se, lane, ev, rk);
     const bool bad = __syncthreads_or(wbad) != 0;
     int* sync_flag = reinterpret_cast<int*>(base + L.bar_off + 12);  // spare word of warp 0's barrier slot
-    l4_dispatch<NW>(base, sync_flag, d, p.id_out, p.T, sb, se, ev, bad);
+    l4_dispatch<NW>(base, sync_flag, d, p.id_out, p.T, sb, se, ev, rk,
+                    reinterpret_cast<const uint32_t*>(base + L.bar_off + 16 + 12), bad);
   }
 }
 
