@@ -311,6 +311,7 @@ __device__ __forceinline__ void l4_dispatch(uint8_t* base, int* sflag, const Dis
   int* slstart = sfirst + E;    // [E] its first position in the staging buffer
   int* wsum = slstart + E;      // [E / 32] scan partials
   int* wsuml = wsum + E / 32;   // [E / 32] scan partials of the staging positions
+  int* sblk = wsuml + E / 32;   // [E + 1] first block of each run, blocks of all runs
   uint32_t* ws = d.ws;
   const long long ngmax = dispatch_groups(d.max_ctas);
   uint32_t* rows = ws + dispatch_rows_word(d.max_ctas);
@@ -470,8 +471,8 @@ __device__ __forceinline__ void l4_dispatch(uint8_t* base, int* sflag, const Dis
       bef += pbef[j * E + tid];
     }
   }
-  const int padded = tid < E ? (tot + d.bs - 1) / d.bs * d.bs : 0;
-  int incl = padded;  // inclusive scan over the experts (warps 0 .. E/32 - 1)
+  const int nblk = tid < E ? (tot + d.bs - 1) / d.bs : 0;  // blocks of the expert's run
+  int incl = nblk;  // inclusive scan over the experts (warps 0 .. E/32 - 1), in blocks
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
     const int v = __shfl_up_sync(0xFFFFFFFFu, incl, o);
@@ -482,11 +483,16 @@ __device__ __forceinline__ void l4_dispatch(uint8_t* base, int* sflag, const Dis
   if (tid < E) {
     int off = 0;
     for (int w = 0; w < warp; ++w) off += wsum[w];
-    const int start = off + incl - padded;
+    const int b0 = off + incl - nblk;
+    const int start = b0 * d.bs;
+    sblk[tid] = b0;
     sstart[tid] = start;
     stot[tid] = tot;
     sfirst[tid] = start + bef;
-    if (tid == E - 1) sstart[E] = off + incl;
+    if (tid == E - 1) {
+      sblk[E] = off + incl;
+      sstart[E] = (off + incl) * d.bs;
+    }
   }
   __syncthreads();
   const int end = sstart[E];
@@ -494,17 +500,17 @@ __device__ __forceinline__ void l4_dispatch(uint8_t* base, int* sflag, const Dis
 
   // 4. shared by the grid: run padding (expert e by CTA e % grid), the slots
   // after the last run and the expert of every block
-  // (runs start on block boundaries: every padded total is a multiple of bs)
   const int32_t numel = static_cast<int32_t>(T * kPairKMax);
   for (int e = c; e < E; e += gridDim.x) {
     const int from = sstart[e] + stot[e], to = sstart[e + 1];
     for (int j = from + tid; j < to; j += NT) d.sorted[j] = numel;
-    for (int b = sstart[e] / d.bs + tid; b < to / d.bs; b += NT) d.expert_ids[b] = e;
+    const int b1 = sblk[e + 1];
+    for (int b = sblk[e] + tid; b < b1; b += NT) d.expert_ids[b] = e;
   }
   const long long gtid = static_cast<long long>(c) * NT + tid;
   const long long gthreads = static_cast<long long>(gridDim.x) * NT;
   for (long long j = end + gtid; j < d.sorted_cap; j += gthreads) d.sorted[j] = numel;
-  for (long long b = end / d.bs + gtid; b < d.eid_cap; b += gthreads) d.expert_ids[b] = -1;
+  for (long long b = sblk[E] + gtid; b < d.eid_cap; b += gthreads) d.expert_ids[b] = -1;
 
   // 5. the CTA's entries to their places: staged entry j of expert e goes
   // to sfirst[e] + (j - slstart[e]), so each expert's entries land in one
