@@ -11,6 +11,7 @@ from .ops import (  # noqa: F401
     gemm_swiglu,
     grouped_topk,
     grouped_topk_exact_rows,
+    grouped_topk_moe_align,
     interleave_gate_up,
     mm_nt,
     rms_norm,
@@ -19,5 +20,5 @@ from .ops import (  # noqa: F401
     silu_and_mul,
 )
 
-__all__ = ["grouped_topk", "grouped_topk_exact_rows", "silu_and_mul", "rms_norm", "mm_nt",
+__all__ = ["grouped_topk", "grouped_topk_exact_rows", "grouped_topk_moe_align", "silu_and_mul", "rms_norm", "mm_nt",
            "gemm_swiglu", "interleave_gate_up", "device_error", "sigmoid", "silu"]
