@@ -457,10 +457,11 @@ static cudaError_t launch_lanes4(const Params& p, cudaStream_t st, EncodeTiledFn
           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return cudaErrorInvalidValue;
+  // one CTA per SM, as many CTAs as tiles up to the SM count: a small batch
+  // runs a few warps on each of many SMs rather than many warps on a few
   const long long wtiles = (p.T + kL4Tokens - 1) / kL4Tokens;
-  const long long ctas_needed = (wtiles + NW - 1) / NW;
-  const long long cap = grid_req > 0 ? grid_req : device_sms();  // one CTA per SM
-  const int grid = static_cast<int>(ctas_needed < cap ? ctas_needed : cap);
+  const long long cap = grid_req > 0 ? grid_req : device_sms();
+  const int grid = static_cast<int>(wtiles < cap ? wtiles : cap);
   const int vec_out = reinterpret_cast<uintptr_t>(p.w_out) % 8 == 0 && reinterpret_cast<uintptr_t>(p.id_out) % 8 == 0;
   if constexpr (kDispatch) {
     cudaLaunchConfig_t cfg = {};
@@ -741,8 +742,7 @@ bool fused_dispatch_applies(const router::Params& p, bool fast, int sms) {
   if (getenv("MCPU_ROUTER_NO_TMA") || getenv("MCPU_DISPATCH_UNFUSED")) return false;
   if (!driver_entry("cuTensorMapEncodeTiled")) return false;
   const long long wtiles = (p.T + router::kL4Tokens - 1) / router::kL4Tokens;
-  const long long ctas = (wtiles + router::kL4Warps - 1) / router::kL4Warps;
-  const long long grid = ctas < sms ? ctas : sms;
+  const long long grid = wtiles < sms ? wtiles : sms;  // the launch's grid (launch_lanes4)
   return (wtiles + grid - 1) / grid <= router::kL4DispatchMaxTiles;
 }
 

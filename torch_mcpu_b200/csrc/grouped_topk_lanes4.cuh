@@ -547,8 +547,11 @@ __global__ void __launch_bounds__(NW * 32, 1) grouped_topk_lanes4_kernel(
   const int q = lane >> 3;        // quarter: groups 2q, 2q + 1
   const int rowoff = t * 128;     // the token's row in every group box
   const int x7 = t << 4;          // its 128-byte swizzle (row t of the atom)
-  // tiles tfirst, tfirst + tstep, ... below tend: round-robin over the grid,
-  // or (dispatch) a contiguous run of the CTA's contiguous range [c0, c1)
+  // tiles tfirst, tfirst + tstep, ... below tend: round-robin over every
+  // warp of the grid -- with at most one tile per warp, consecutive tiles on
+  // different CTAs (a small batch spreads over as many SMs as it has tiles),
+  // else consecutive tiles on one CTA's warps -- or (dispatch) a contiguous
+  // run of the CTA's contiguous range [c0, c1)
   long long tfirst, tstep, tend;
   if constexpr (kDispatch) {
     const long long c0 = static_cast<long long>(blockIdx.x) * wtiles / gridDim.x;
@@ -558,17 +561,22 @@ __global__ void __launch_bounds__(NW * 32, 1) grouped_topk_lanes4_kernel(
     tstep = 1;
     tend = tfirst + tpw < c1 ? tfirst + tpw : c1;
   } else {
-    tfirst = static_cast<long long>(blockIdx.x) * NW + warp;
     tstep = static_cast<long long>(gridDim.x) * NW;
+    tfirst = wtiles <= tstep ? static_cast<long long>(warp) * gridDim.x + blockIdx.x
+                             : static_cast<long long>(blockIdx.x) * NW + warp;
     tend = wtiles;
   }
   const float* gating = static_cast<const float*>(p.gating);
 
+  // the logits are read once: first out of L2, so that they do not evict
+  // the outputs, the workspace and this kernel's instructions
+  const uint64_t stream_policy = sm100::l2_evict_first_policy();
   auto issue = [&](long long wt) {
     if (lane == 0) sm100::mbar_arrive_expect_tx(full, kL4Tile);
     __syncwarp();
     if (lane < kPairG)
-      sm100::tma_load_2d(tb + lane * kL4Box, &tm, full, lane * kPairGS, static_cast<int>(wt * kL4Tokens));
+      sm100::tma_load_2d_hint(tb + lane * kL4Box, &tm, full, lane * kPairGS, static_cast<int>(wt * kL4Tokens),
+                              stream_policy);
   };
 
   if (lane == 0) {
