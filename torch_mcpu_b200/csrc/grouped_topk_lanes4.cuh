@@ -341,20 +341,22 @@ __device__ __forceinline__ void l4_dispatch(uint8_t* base, int* sflag, const Dis
 #pragma unroll
     for (int j = 0; j < Q; ++j) h += psum[j * E + tid];
   }
-  // staging positions: exclusive scan of h over the experts (warps 0 .. 7)
-  int hincl = h;
+  // (the expert threads, warps 0 .. E/32 - 1, only: the other warps would
+  // share their issue slots) staging positions: exclusive scan of h over
+  // the experts; the CTA's row and group sum
+  if (tid < E) {
+    int hincl = h;
 #pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int v = __shfl_up_sync(0xFFFFFFFFu, hincl, o);
-    if (lane >= o) hincl += v;
-  }
-  if (tid < E && lane == 31) wsuml[warp] = hincl;
-  if (tid < E) slstart[tid] = hincl - h;  // within its group of 32 experts until the offsets below
-  {
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xFFFFFFFFu, hincl, o);
+      if (lane >= o) hincl += v;
+    }
+    if (lane == 31) wsuml[warp] = hincl;
+    slstart[tid] = hincl - h;  // within its group of 32 experts until the offsets below
     const uint32_t hn = __shfl_down_sync(0xFFFFFFFFu, static_cast<uint32_t>(h), 1);
-    if (tid < E && (tid & 1) == 0)
+    if ((tid & 1) == 0)
       rows[static_cast<long long>(c) * (E / 2) + (tid >> 1)] = static_cast<uint32_t>(h) | (hn << 16);
-    if (tid < E && h != 0) atomicAdd(gs_cur + static_cast<long long>(gi) * E + tid, static_cast<uint32_t>(h));
+    if (h != 0) atomicAdd(gs_cur + static_cast<long long>(gi) * E + tid, static_cast<uint32_t>(h));
   }
   // 2. arrive (release: the CTA's row and group sum); while the other CTAs
   // arrive, the per-warp offsets within the CTA and the CTA's entries sorted
@@ -471,14 +473,17 @@ __device__ __forceinline__ void l4_dispatch(uint8_t* base, int* sflag, const Dis
       bef += pbef[j * E + tid];
     }
   }
-  const int nblk = tid < E ? (tot + d.bs - 1) / d.bs : 0;  // blocks of the expert's run
-  int incl = nblk;  // inclusive scan over the experts (warps 0 .. E/32 - 1), in blocks
+  int nblk = 0, incl = 0;
+  if (tid < E) {  // inclusive scan over the experts (warps 0 .. E/32 - 1), in blocks
+    nblk = (tot + d.bs - 1) / d.bs;  // blocks of the expert's run
+    incl = nblk;
 #pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int v = __shfl_up_sync(0xFFFFFFFFu, incl, o);
-    if (lane >= o) incl += v;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    if (lane == 31) wsum[warp] = incl;
   }
-  if (tid < E && lane == 31) wsum[warp] = incl;
   __syncthreads();
   if (tid < E) {
     int off = 0;
@@ -500,12 +505,14 @@ __device__ __forceinline__ void l4_dispatch(uint8_t* base, int* sflag, const Dis
 
   // 4. shared by the grid: run padding (expert e by CTA e % grid), the slots
   // after the last run and the expert of every block
+  // (one warp per expert: with 148 CTAs only warps 0 and 1 have an expert,
+  // and the others go straight on instead of sharing the issue slots)
   const int32_t numel = static_cast<int32_t>(T * kPairKMax);
-  for (int e = c; e < E; e += gridDim.x) {
+  for (int e = c + warp * static_cast<int>(gridDim.x); e < E; e += NW * static_cast<int>(gridDim.x)) {
     const int from = sstart[e] + stot[e], to = sstart[e + 1];
-    for (int j = from + tid; j < to; j += NT) d.sorted[j] = numel;
+    for (int j = from + lane; j < to; j += 32) d.sorted[j] = numel;
     const int b1 = sblk[e + 1];
-    for (int b = sblk[e] + tid; b < b1; b += NT) d.expert_ids[b] = e;
+    for (int b = sblk[e] + lane; b < b1; b += 32) d.expert_ids[b] = e;
   }
   const long long gtid = static_cast<long long>(c) * NT + tid;
   const long long gthreads = static_cast<long long>(gridDim.x) * NT;
